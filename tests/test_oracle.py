@@ -1,0 +1,50 @@
+"""The CPU oracle reproduces the reference's own outputs (golden fixtures made by importing the reference)."""
+
+import numpy as np
+import pytest
+
+from golden_io import CASES, load
+from oracle import OracleConfig, OracleModel
+
+
+def oracle_for(g):
+    m = g["meta"]
+    return OracleModel(OracleConfig(**m["cfg"]), g["weights"], k=m["k"], pos_scale=m["pos_scale"])
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_teacher_forced_logits_match_reference(name):
+    g = load(name)
+    om = oracle_for(g)
+    offs = np.concatenate([[0], np.cumsum(g["meta"]["lens"])])
+    for b in range(len(g["meta"]["lens"])):
+        got = om.logits(g["frames"][offs[b]:offs[b + 1]], g["tf_tokens"][b])
+        np.testing.assert_allclose(got, g["tf_logits"][b], atol=2e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_greedy_tokens_match_reference(name):
+    g = load(name)
+    m = g["meta"]
+    om = oracle_for(g)
+    out, margin = om.generate(g["frames"], m["lens"], m["max_new"], steps=m["max_new"], bias=g["bias"],
+                              max_homopolymer=m["max_homopolymer"])
+    np.testing.assert_array_equal(out, g["tokens"])
+    # every decided token had a clear fp32 margin, so the comparison is meaningful
+    assert np.nanmin(margin) > 1e-4
+
+
+def test_tokenizer_matches_reference_layout():
+    from viktor_b200.config import EOS, KmerTokenizer
+    import random
+    for k in (1, 4):
+        tok = KmerTokenizer(k)
+        assert tok.vocab_size == 3 + sum(4 ** j for j in range(1, k + 1))
+        rng = random.Random(k)
+        for n in range(0, 23):
+            s = "".join(rng.choice("ACGT") for _ in range(n))
+            ids = tok.encode(s)
+            assert len(ids) == -(-n // k)
+            assert not any(tok.tail_mask[i] for i in ids[:-1])
+            assert tok.decode(ids + [EOS, 5]) == s
+            assert int(tok.n_bases[ids].sum()) == n
