@@ -1,0 +1,149 @@
+/*
+ * viktor_b200 -- C ABI of the B200 (sm_100a) decoder inference kernels.
+ *
+ * Every entry point takes plain device pointers, sizes and strides, launches on the given CUDA stream
+ * (cudaStream_t passed as void*, NULL = legacy default stream) and returns an int status.  Nothing here
+ * allocates device memory or synchronises the host, so every call can be captured into a CUDA graph; the
+ * caller owns all buffers, including the decode-attention workspace.
+ *
+ * Data types: "bf16" buffers hold __nv_bfloat16, "f32" float, "i32" int32_t, "i64" int64_t, "u8" uint8_t.
+ * Layouts are row-major and contiguous unless a stride is given.  The decoder geometry the kernels are built
+ * for is the Viktor decoder: d_model 512, 8 query heads, 2 KV heads, head_dim 64 (GQA group 4).
+ *
+ * Each function names the reference interface (GHSSHG/Viktor, path:line) whose semantics it implements.
+ */
+#ifndef VIKTOR_B200_H
+#define VIKTOR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------------------------------------------- */
+#define VK_OK 0
+#define VK_ERR_ARG (-1)         /* unsupported shape, null or misaligned pointer, bad size */
+#define VK_ERR_CUDA (-2)        /* a CUDA launch or runtime call failed */
+#define VK_ERR_UNSUPPORTED (-3) /* geometry the kernels are not built for */
+
+/* Device error word bits (set by kernels, read with vk_read_device_errors). */
+#define VK_DEVERR_WAIT_FULL 1u   /* a consumer gave up waiting for a TMA stage */
+#define VK_DEVERR_WAIT_EMPTY 2u  /* a producer gave up waiting for a free stage */
+#define VK_DEVERR_WAIT_ACCUM 4u  /* an epilogue gave up waiting for the tensor-core accumulator */
+#define VK_DEVERR_BOUNDS 8u      /* an index (token, position, cache row) was out of range; access skipped */
+
+/* Library version as major*10000 + minor*100 + patch. */
+int vk_version(void);
+
+/* Reads (and with clear != 0, clears) the device error word of the current device.  Synchronous. */
+int vk_read_device_errors(uint32_t* bits, int clear);
+
+/* Enables (1) or disables (0) programmatic dependent launch between consecutive kernels.  Default 1. */
+int vk_set_pdl(int enable);
+
+/* ---- fused row ops: viktor/triton_ops.py ------------------------------------------------------------------ */
+
+/* viktor/triton_ops.py:34-40 add_rmsnorm.  x [n, d] bf16 (updated in place by += delta when delta != NULL),
+ * w [d] bf16, h [n, d] bf16 out: h = RMSNorm(x) * w.  d in {512}. */
+int vk_add_rmsnorm(void* x, const void* delta, const void* w, void* h, int64_t n, int d, float eps,
+                   void* stream);
+
+/* viktor/triton_ops.py:163-169 embed_rmsnorm.  tok [n] i64, emb [V, d] bf16, w [d]; x, h [n, d] bf16 out. */
+int vk_embed_rmsnorm(const int64_t* tok, const void* emb, int64_t vocab, const void* w, void* x, void* h,
+                     int64_t n, int d, float eps, void* stream);
+
+/* viktor/triton_ops.py:94-108 qkv_rope_cache.  qkv [n, (H + 2 Hkv) * 64] bf16; q_norm_w, k_norm_w [64] bf16;
+ * cos, sin [rope_len, 32] f32; pos, seq [n] i32 (cache position and cache row of each token); rope_pos [n] i32
+ * or NULL (= pos); q [n, H, 64] bf16 out; k_cache, v_cache: one layer, element (row, p, kvh, d) at
+ * row * stride_cb + p * stride_cs + kvh * 64 + d; k_out, v_out [n, Hkv, 64] bf16 or NULL. */
+int vk_qkv_rope_cache(const void* qkv, const void* q_norm_w, const void* k_norm_w, const float* cos,
+                      const float* sin, int rope_len, const int32_t* pos, const int32_t* rope_pos,
+                      const int32_t* seq, void* q, void* k_cache, void* v_cache, void* k_out, void* v_out,
+                      int64_t n, int64_t stride_cb, int64_t stride_cs, int cache_rows, int cache_len, float eps,
+                      int n_heads, int n_kv_heads, int head_dim, void* stream);
+
+/* viktor/triton_ops.py:138-146 linear, on tcgen05 tensor cores.  x [M, K] bf16, w [N, K] bf16 (nn.Linear
+ * layout).  swiglu = 0: y [M, N] (bf16, or f32 when out_f32).  swiglu = 1: w is gate_up with N = 2F rows (gate
+ * rows first) and y [M, F] bf16 = silu(gate) * up.  K a multiple of 64; with swiglu, F a multiple of 32
+ * (M <= 4096) or 128 (larger M). */
+int vk_linear(const void* x, const void* w, void* y, int64_t M, int N, int K, int swiglu, int out_f32,
+              void* stream);
+
+/* viktor/triton_ops.py:223-229 swiglu.  gu [n, 2F] bf16 (gate | up) -> out [n, F] bf16. */
+int vk_swiglu(const void* gu, void* out, int64_t n, int F, void* stream);
+
+/* viktor/triton_ops.py:200-209 greedy_update (+ viktor/engine.py:79-89 _select at temperature 0).
+ * logits [B, V] f32 (row stride ld_logits); bias [V] f32; is_tail, is_homo [V] u8; tok, run, pos, plen,
+ * rope_off [B] i64; out [B, out_cols] i64 (row stride out_stride); pos32, seqlens, rpos32 [B] i32.
+ * When emb != NULL, additionally writes x = emb[new tok] and h = RMSNorm(x) * norm_w ([B, 512] bf16) for
+ * the next decode step (the embed_rmsnorm of viktor/fast_decoder.py:80-81, fused). */
+int vk_greedy_update(const float* logits, int64_t ld_logits, const float* bias, const uint8_t* is_tail,
+                     const uint8_t* is_homo, int homo_stop, int64_t* tok, int64_t* run, int64_t* pos,
+                     const int64_t* plen, const int64_t* rope_off, int64_t* out, int64_t out_stride,
+                     int64_t out_cols, int32_t* pos32, int32_t* seqlens, int32_t* rpos32, int B, int V, int eos,
+                     int pad, const void* emb, const void* norm_w, void* x, void* h, float eps, void* stream);
+
+/* ---- attention: viktor/decode_attention.py, flash_attn calls of viktor/fast_decoder.py ------------------- */
+
+/* Workspace bytes vk_decode_attention needs for nq queries over a cache of S positions. */
+size_t vk_decode_attention_workspace_bytes(int nq, int S);
+
+/* viktor/decode_attention.py:41-53 decode_attention (and flash_attn_with_kvcache, viktor/fast_decoder.py:88).
+ * q [nq, 8, 64] bf16; k_cache/v_cache: one layer, (row, p, kvh, d) at row * stride_kb + p * stride_ks +
+ * kvh * 64 + d with stride_ks >= 128; query i attends cache row row0 + i, positions [0, lengths[i]),
+ * 1 <= lengths[i] <= S (i32); out [nq, 8, 64] bf16.  workspace: vk_decode_attention_workspace_bytes(nq, S)
+ * bytes, 16-byte aligned, ZERO-FILLED once before first use (it holds per-query tickets that every call
+ * returns to zero). */
+int vk_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* lengths,
+                        void* out, int nq, int row0, int cache_rows, int S, int64_t stride_kb, int64_t stride_ks,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* flash_attn_varlen_func(q, k, v, cu, cu, max_len, max_len, causal=True) of viktor/fast_decoder.py:73, with K
+ * and V read from the cache rows the prefill just wrote.  q, out [n_tok, 8, 64] bf16 packed by cu_seqlens
+ * [nseq + 1] (i32, device); sequence b attends cache row row0 + b, positions [0, T_b).  max_seqlen = max T_b. */
+int vk_prefill_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* cu_seqlens,
+                         int nseq, int max_seqlen, int64_t n_tok, int row0, int cache_rows, int S,
+                         int64_t stride_kb, int64_t stride_ks, void* out, void* stream);
+
+/* ---- tensor-core projections with fused epilogues (the B200 forms of viktor/fast_decoder.py:33-60) ------- */
+
+/* h [M, 512] bf16 . w_qkv [(H + 2 Hkv) * 64, 512]^T followed by the qkv_rope_cache epilogue (arguments as in
+ * vk_qkv_rope_cache).  Replaces linear + qkv_rope_cache of viktor/fast_decoder.py:44-47. */
+int vk_linear_qkv_rope_cache(const void* h, const void* w_qkv, const void* q_norm_w, const void* k_norm_w,
+                             const float* cos, const float* sin, int rope_len, const int32_t* pos,
+                             const int32_t* rope_pos, const int32_t* seq, void* q, void* k_cache, void* v_cache,
+                             void* k_out, void* v_out, int64_t M, int64_t stride_cb, int64_t stride_cs,
+                             int cache_rows, int cache_len, float eps, int n_heads, int n_kv_heads,
+                             void* stream);
+
+/* a [M, K] bf16 . w [512, K]^T = delta, then x += delta (bf16, in place) and h = RMSNorm(x) * norm_w
+ * ([M, 512] bf16).  Replaces mm + add_rmsnorm of viktor/fast_decoder.py:55,57-59.  K a multiple of 64. */
+int vk_linear_add_rmsnorm(const void* a, const void* w, void* x, const void* norm_w, void* h, int64_t M, int K,
+                          float eps, void* stream);
+
+/* y = act(x [M, K] . w [N, K]^T + bias) as bf16; act 0 = identity, 1 = GELU (erf).  Row i of the result goes
+ * to row row_map[i] of y (row_map NULL = identity; ldy = row stride of y).  The projector of
+ * viktor/model.py:35 and the packed-prefill scatter of viktor/engine.py:163-164. */
+int vk_linear_bias_act(const void* x, const void* w, const void* bias, void* y, int64_t ldy,
+                       const int32_t* row_map, int64_t M, int N, int K, int act, void* stream);
+
+/* ---- layout helpers --------------------------------------------------------------------------------------- */
+int vk_cast_f32_bf16(const float* src, void* dst, int64_t n, void* stream);
+/* dst[i, :] = src[idx[i], :] for rows of row_bytes (multiple of 16), src has src_rows rows. */
+int vk_gather_rows(const void* src, const int64_t* idx, void* dst, int64_t n, int row_bytes, int64_t src_rows,
+                   void* stream);
+/* dst[dst_idx[i], :] = src[src_idx[i], :] for rows of row_bytes (multiple of 16); a NULL index is the
+ * identity.  Indices are i64 and bounds-checked against src_rows / dst_rows. */
+int vk_copy_rows(const void* src, const int64_t* src_idx, int64_t src_rows, void* dst, const int64_t* dst_idx,
+                 int64_t dst_rows, int64_t n, int row_bytes, void* stream);
+/* x[rows[i], :] = emb[token, :] (d bf16 values per row). */
+int vk_scatter_embed(void* x, const int64_t* rows, int64_t n, int64_t x_rows, const void* emb, int64_t token,
+                     int d, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VIKTOR_B200_H */

@@ -1,0 +1,144 @@
+"""End-to-end parity of the B200 engine against the reference (golden fixtures) and the CPU oracle.
+
+* Teacher-forced logits (all layers over [frames | tokens]) agree with the reference's fp32 logits within
+  max-abs 3e-2 (bf16 storage between ops, the same rounding points as the reference's Triton path).
+* Greedy tokens equal the reference's, per chunk, up to the first step whose fp32 top-2 logit margin is below
+  the bf16 noise floor (0.05); from there on a bf16 path may legitimately pick the other token.
+* The CUDA-graph decode equals the eager decode token for token.
+* At the benchmark size (256 chunks x 2048 frames) the results are batch-invariant (a chunk decodes to the
+  same tokens inside the full batch as alone) and agree with the oracle on sampled chunks.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from golden_io import load
+from oracle import OracleConfig, OracleModel
+
+pytestmark = pytest.mark.gpu
+
+MARGIN_FLOOR = 0.05
+CASES = ["base_theta1e6", "base_theta1e4", "kmer4", "homopolymer", "pos_scale2", "base_b8"]
+
+
+@pytest.fixture(autouse=True)
+def _errors_clear():
+    from viktor_b200._lib import check_device_errors
+    yield
+    torch.cuda.synchronize()
+    check_device_errors()
+
+
+def build(g, B=None, max_new=None, graph=True, max_frames=None):
+    from viktor_b200 import Basecaller, DecodeEngine, DecoderConfig
+    m = g["meta"]
+    model = Basecaller.from_weights(g["weights"], k=m["k"], cfg=DecoderConfig(**m["cfg"]), d_enc=m["d_enc"],
+                                    pos_scale=m["pos_scale"])
+    eng = DecodeEngine(model, B or len(m["lens"]), max_new or m["max_new"], max_frames or max(m["lens"]),
+                       cuda_graph=graph, max_homopolymer=m["max_homopolymer"], device="cuda")
+    eng.bias.copy_(torch.from_numpy(g["bias"]))
+    return eng
+
+
+def agree_until_low_margin(got, ref, margin):
+    """Per row: True if tokens agree at every step before the first step with margin < floor."""
+    ok = []
+    for b in range(ref.shape[0]):
+        low = np.where(np.nan_to_num(margin[b], nan=np.inf) < MARGIN_FLOOR)[0]
+        stop = int(low[0]) if len(low) else ref.shape[1]
+        ok.append(np.array_equal(got[b, :stop], ref[b, :stop]))
+    return np.array(ok)
+
+
+def oracle_for(g):
+    m = g["meta"]
+    return OracleModel(OracleConfig(**m["cfg"]), g["weights"], k=m["k"], pos_scale=m["pos_scale"])
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_teacher_forced_logits_match_reference(name):
+    g = load(name)
+    m = g["meta"]
+    eng = build(g, max_new=g["tf_tokens"].shape[1], graph=False)
+    got = eng.teacher_forced_logits(torch.from_numpy(g["frames"]), m["lens"],
+                                    torch.from_numpy(g["tf_tokens"])).cpu().numpy()
+    err = np.abs(got - g["tf_logits"]).max()
+    assert err < 3e-2, f"max |logits - reference fp32| = {err}"
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_greedy_tokens_match_reference(name):
+    g = load(name)
+    m = g["meta"]
+    eng = build(g)
+    got = eng.generate(torch.from_numpy(g["frames"]), m["lens"], m["max_new"]).cpu().numpy()
+    _, margin = oracle_for(g).generate(g["frames"], m["lens"], m["max_new"], steps=m["max_new"], bias=g["bias"],
+                                       max_homopolymer=m["max_homopolymer"])
+    ok = agree_until_low_margin(got, g["tokens"], margin)
+    assert ok.all(), f"rows disagreeing before a low-margin step: {np.where(~ok)[0]}\n{got}\n{g['tokens']}"
+    exact = (got == g["tokens"]).all(1).mean()
+    print(f"{name}: identical rows {exact:.3f}")
+
+
+def test_graph_equals_eager():
+    g = load("base_b8")
+    m = g["meta"]
+    frames = torch.from_numpy(g["frames"])
+    a = build(g, graph=True).generate(frames, m["lens"], m["max_new"]).clone()
+    b = build(g, graph=False).generate(frames, m["lens"], m["max_new"]).clone()
+    assert torch.equal(a, b)
+
+
+def test_engine_reuse_and_decode_until_done():
+    """A second generate() on the same engine reproduces the first; steps=None stops early once every row
+    emitted EOS (default grammar, EOS not masked) and fills the rest with PAD."""
+    g = load("base_theta1e4")
+    m = g["meta"]
+    eng = build(g)
+    frames = torch.from_numpy(g["frames"])
+    a = eng.generate(frames, m["lens"], m["max_new"]).clone()
+    b = eng.generate(frames, m["lens"], m["max_new"]).clone()
+    assert torch.equal(a, b)
+    c = eng.generate(frames, m["lens"], None).clone()
+    assert torch.equal(c, a)
+
+
+@pytest.fixture(scope="module")
+def full_size():
+    """The benchmark configuration: 256 chunks of 2048 frames, BASELINE architecture, torch-default init."""
+    from viktor_b200 import Basecaller, DecodeEngine, DecoderConfig
+    from viktor_b200.synthetic import make_frames, make_weights
+    cfg = DecoderConfig(vocab_size=7, rope_theta=1e6)
+    weights = make_weights(cfg, seed=21, init="torch")
+    lens = [2048] * 256
+    frames = make_frames(lens, seed=22)
+    model = Basecaller.from_weights(weights, k=1, cfg=cfg)
+    steps = 12
+    eng = DecodeEngine(model, 256, steps, 2048, max_homopolymer=None, device="cuda")
+    eng.bias[2] = float("-inf")
+    out = eng.generate(torch.from_numpy(frames), lens, steps).cpu().numpy()
+    return dict(weights=weights, frames=frames, lens=lens, out=out, steps=steps, model=model, cfg=cfg, eng=eng)
+
+
+def test_full_size_batch_invariance(full_size):
+    from viktor_b200 import DecodeEngine
+    f = full_size
+    pick = [0, 77, 200, 255]
+    eng = DecodeEngine(f["model"], len(pick), f["steps"], 2048, max_homopolymer=None, device="cuda")
+    eng.bias[2] = float("-inf")
+    sub = np.concatenate([f["frames"][2048 * b:2048 * (b + 1)] for b in pick])
+    got = eng.generate(torch.from_numpy(sub), [2048] * len(pick), f["steps"]).cpu().numpy()
+    assert np.array_equal(got, f["out"][pick])
+
+
+def test_full_size_matches_oracle_on_samples(full_size):
+    f = full_size
+    pick = [3, 150]
+    om = OracleModel(OracleConfig(vocab_size=7, rope_theta=1e6), f["weights"], k=1)
+    bias = np.zeros(7, np.float32)
+    bias[[0, 1, 2]] = -np.inf
+    sub = np.concatenate([f["frames"][2048 * b:2048 * (b + 1)] for b in pick])
+    ref, margin = om.generate(sub, [2048] * len(pick), f["steps"], steps=f["steps"], bias=bias, max_homopolymer=None)
+    ok = agree_until_low_margin(f["out"][pick], ref, margin)
+    assert ok.all(), f"\n{f['out'][pick]}\n{ref}\n{margin}"

@@ -1,0 +1,339 @@
+// Row-wise kernels of the decoder path: RMSNorm variants, the standalone QK-norm/RoPE/cache op, SwiGLU,
+// greedy token selection with its grammar, and small layout kernels (cast, gather, scatter).
+// Rounding follows the reference: bf16 storage between ops, fp32 math inside an op
+// (viktor/triton_ops.py:9).
+#pragma once
+
+#include "vk_common.cuh"
+
+namespace vk {
+namespace ew {
+
+VK_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// One warp per row, d a multiple of 256 (each lane holds d/32 elements as 16-byte chunks).
+// x = bf16(x + delta) in place (if delta), h = bf16(x * rsqrt(mean(x^2) + eps) * w)   (viktor/triton_ops.py:17-31)
+// With tok != nullptr the row is first replaced by emb[tok[row]] (viktor/triton_ops.py:149-160).
+template <int D>
+__global__ void __launch_bounds__(256) rmsnorm_rows_kernel(__nv_bfloat16* x, const __nv_bfloat16* delta,
+                                                           const int64_t* tok, const __nv_bfloat16* emb,
+                                                           int64_t vocab, const __nv_bfloat16* w,
+                                                           __nv_bfloat16* h, int64_t n, float eps) {
+  constexpr int PER = D / 32;  // elements per lane
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  pdl_wait();
+  if (row >= n) return;
+  float v[PER];
+  __nv_bfloat16* xr = x + row * D;
+  const __nv_bfloat16* src = xr;
+  if (tok) {
+    int64_t t = tok[row];
+    if (t < 0 || t >= vocab) {
+      if (lane == 0) raise_error(ERR_BOUNDS);
+      t = 0;
+    }
+    src = emb + t * D;
+  }
+#pragma unroll
+  for (int c = 0; c < PER / 8; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    uint4 u = *reinterpret_cast<const uint4*>(src + col);
+    v[c * 8 + 0] = bf16_lo(u.x); v[c * 8 + 1] = bf16_hi(u.x);
+    v[c * 8 + 2] = bf16_lo(u.y); v[c * 8 + 3] = bf16_hi(u.y);
+    v[c * 8 + 4] = bf16_lo(u.z); v[c * 8 + 5] = bf16_hi(u.z);
+    v[c * 8 + 6] = bf16_lo(u.w); v[c * 8 + 7] = bf16_hi(u.w);
+    if (delta) {
+      uint4 dd = *reinterpret_cast<const uint4*>(delta + row * D + col);
+      v[c * 8 + 0] = bf16_round(v[c * 8 + 0] + bf16_lo(dd.x)); v[c * 8 + 1] = bf16_round(v[c * 8 + 1] + bf16_hi(dd.x));
+      v[c * 8 + 2] = bf16_round(v[c * 8 + 2] + bf16_lo(dd.y)); v[c * 8 + 3] = bf16_round(v[c * 8 + 3] + bf16_hi(dd.y));
+      v[c * 8 + 4] = bf16_round(v[c * 8 + 4] + bf16_lo(dd.z)); v[c * 8 + 5] = bf16_round(v[c * 8 + 5] + bf16_hi(dd.z));
+      v[c * 8 + 6] = bf16_round(v[c * 8 + 6] + bf16_lo(dd.w)); v[c * 8 + 7] = bf16_round(v[c * 8 + 7] + bf16_hi(dd.w));
+    }
+    if (delta || tok) {
+      uint4 o;
+      o.x = pack_bf16x2(v[c * 8 + 0], v[c * 8 + 1]);
+      o.y = pack_bf16x2(v[c * 8 + 2], v[c * 8 + 3]);
+      o.z = pack_bf16x2(v[c * 8 + 4], v[c * 8 + 5]);
+      o.w = pack_bf16x2(v[c * 8 + 6], v[c * 8 + 7]);
+      *reinterpret_cast<uint4*>(xr + col) = o;
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) ss += v[i] * v[i];
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+  for (int c = 0; c < PER / 8; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    uint4 wu = *reinterpret_cast<const uint4*>(w + col);
+    float wv[8] = {bf16_lo(wu.x), bf16_hi(wu.x), bf16_lo(wu.y), bf16_hi(wu.y),
+                   bf16_lo(wu.z), bf16_hi(wu.z), bf16_lo(wu.w), bf16_hi(wu.w)};
+    uint4 o;
+    o.x = pack_bf16x2(v[c * 8 + 0] * r * wv[0], v[c * 8 + 1] * r * wv[1]);
+    o.y = pack_bf16x2(v[c * 8 + 2] * r * wv[2], v[c * 8 + 3] * r * wv[3]);
+    o.z = pack_bf16x2(v[c * 8 + 4] * r * wv[4], v[c * 8 + 5] * r * wv[5]);
+    o.w = pack_bf16x2(v[c * 8 + 6] * r * wv[6], v[c * 8 + 7] * r * wv[7]);
+    *reinterpret_cast<uint4*>(h + row * D + col) = o;
+  }
+  pdl_launch_dependents();
+}
+
+// Standalone QK-norm + RoPE + cache write (viktor/triton_ops.py:52-108): one thread per (token, head).
+__global__ void __launch_bounds__(128) qkv_rope_cache_kernel(
+    const __nv_bfloat16* qkv, const __nv_bfloat16* qw, const __nv_bfloat16* kw, const float* cos, const float* sin,
+    int rope_len, const int32_t* pos, const int32_t* rope_pos, const int32_t* seq, __nv_bfloat16* q,
+    __nv_bfloat16* kc, __nv_bfloat16* vc, __nv_bfloat16* ko, __nv_bfloat16* vo, int64_t n, int64_t stride_cb,
+    int64_t stride_cs, int cache_rows, int cache_len, float eps, int H, int HKV) {
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int NH = H + 2 * HKV;
+  pdl_wait();
+  if (gid >= n * NH) return;
+  const int64_t t = gid / NH;
+  const int hd = static_cast<int>(gid % NH);
+  const int p = pos[t], rp = rope_pos ? rope_pos[t] : p, sq = seq[t];
+  if (p < 0 || p >= cache_len || sq < 0 || sq >= cache_rows || rp < 0 || rp >= rope_len) {
+    raise_error(ERR_BOUNDS);
+    return;
+  }
+  float v[64];
+  const __nv_bfloat16* src = qkv + (t * NH + hd) * 64;
+#pragma unroll
+  for (int i = 0; i < 64; i += 8) {
+    uint4 u = *reinterpret_cast<const uint4*>(src + i);
+    v[i] = bf16_lo(u.x); v[i + 1] = bf16_hi(u.x); v[i + 2] = bf16_lo(u.y); v[i + 3] = bf16_hi(u.y);
+    v[i + 4] = bf16_lo(u.z); v[i + 5] = bf16_hi(u.z); v[i + 6] = bf16_lo(u.w); v[i + 7] = bf16_hi(u.w);
+  }
+  auto store64 = [&](__nv_bfloat16* dst) {
+#pragma unroll
+    for (int i = 0; i < 64; i += 8) {
+      uint4 o;
+      o.x = pack_bf16x2(v[i], v[i + 1]); o.y = pack_bf16x2(v[i + 2], v[i + 3]);
+      o.z = pack_bf16x2(v[i + 4], v[i + 5]); o.w = pack_bf16x2(v[i + 6], v[i + 7]);
+      *reinterpret_cast<uint4*>(dst + i) = o;
+    }
+  };
+  if (hd < H + HKV) {
+    const __nv_bfloat16* wn = hd < H ? qw : kw;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) ss += v[i] * v[i];
+    const float r = rsqrtf(ss * (1.0f / 64.0f) + eps);
+    const float* cr = cos + static_cast<int64_t>(rp) * 32;
+    const float* sr = sin + static_cast<int64_t>(rp) * 32;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float y1 = bf16_round(v[i] * r * __bfloat162float(wn[i]));
+      const float y2 = bf16_round(v[i + 32] * r * __bfloat162float(wn[i + 32]));
+      v[i] = y1 * cr[i] - y2 * sr[i];
+      v[i + 32] = y1 * sr[i] + y2 * cr[i];
+    }
+  }
+  if (hd < H) {
+    store64(q + (t * H + hd) * 64);
+    return;
+  }
+  const bool is_k = hd < H + HKV;
+  const int kvh = is_k ? hd - H : hd - H - HKV;
+  store64((is_k ? kc : vc) + static_cast<int64_t>(sq) * stride_cb + static_cast<int64_t>(p) * stride_cs + kvh * 64);
+  __nv_bfloat16* packed = is_k ? ko : vo;
+  if (packed) store64(packed + (t * HKV + kvh) * 64);
+}
+
+// silu(gate) * up with the silu output rounded to bf16 (viktor/triton_ops.py:212-220).
+__global__ void swiglu_kernel(const __nv_bfloat16* gu, __nv_bfloat16* out, int64_t n, int F) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  pdl_wait();
+  if (i >= n * F) return;
+  const int64_t row = i / F;
+  const int col = static_cast<int>(i % F);
+  const float g = __bfloat162float(gu[row * 2 * F + col]);
+  const float u = __bfloat162float(gu[row * 2 * F + F + col]);
+  const float act = bf16_round(g * (1.0f / (1.0f + __expf(-g))));
+  out[i] = __float2bfloat16_rn(act * u);
+}
+
+// Greedy selection + grammar + state advance, one CTA (128 threads) per sequence
+// (viktor/triton_ops.py:172-197, viktor/engine.py:79-89).  With x/h set, the chosen token's embedding and its
+// first-layer RMSNorm are written for the next decode step (viktor/triton_ops.py:149-160).
+struct GreedyArgs {
+  const float* logits;
+  int64_t ld_logits;
+  const float* bias;
+  const uint8_t* is_tail;
+  const uint8_t* is_homo;
+  int homo_stop;
+  int64_t* tok;
+  int64_t* run;
+  int64_t* pos;
+  const int64_t* plen;
+  const int64_t* rope_off;
+  int64_t* out;
+  int64_t out_stride;
+  int64_t out_cols;
+  int32_t* pos32;
+  int32_t* seqlens;
+  int32_t* rpos32;
+  int B, V, eos, pad;
+  // optional fused embedding of the chosen token
+  const __nv_bfloat16* emb;
+  const __nv_bfloat16* norm_w;
+  __nv_bfloat16* x;
+  __nv_bfloat16* h;
+  float eps;
+};
+
+template <int D>
+__global__ void __launch_bounds__(128) greedy_kernel(GreedyArgs a) {
+  __shared__ float sv[4];
+  __shared__ int si[4];
+  __shared__ int64_t chosen;
+  __shared__ float sred[4];
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_wait();
+  if (b >= a.B) return;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int v = tid; v < a.V; v += 128) {
+    const float z = a.logits[static_cast<int64_t>(b) * a.ld_logits + v] + a.bias[v];
+    if (z > best || (z == best && v < bi)) {
+      best = z;
+      bi = v;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (ob > best || (ob == best && oi < bi)) {
+      best = ob;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    sv[warp] = best;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < 4; ++w)
+      if (sv[w] > best || (sv[w] == best && si[w] < bi)) {
+        best = sv[w];
+        bi = si[w];
+      }
+    if (bi == 0x7fffffff) bi = 0;
+    int64_t nxt = bi;
+    const int64_t prev = a.tok[b];
+    const bool prev_ok = prev >= 0 && prev < a.V;
+    if (!prev_ok) raise_error(ERR_BOUNDS);
+    if (prev_ok && a.is_tail[prev]) nxt = a.eos;  // a tail must be last
+    if (a.homo_stop > 0) {
+      const bool same = (nxt == prev) && a.is_homo[nxt];
+      const int64_t run = same ? a.run[b] + 1 : 0;
+      a.run[b] = run;
+      if (run + 1 >= a.homo_stop) nxt = a.eos;
+    }
+    if (prev == a.eos || prev == a.pad) nxt = a.pad;
+    int64_t p = a.pos[b];
+    const int64_t col = p - a.plen[b];
+    if (col >= 0 && col < a.out_cols)
+      a.out[static_cast<int64_t>(b) * a.out_stride + col] = nxt;
+    else
+      raise_error(ERR_BOUNDS);
+    a.tok[b] = nxt;
+    p += 1;
+    a.pos[b] = p;
+    a.pos32[b] = static_cast<int32_t>(p);
+    a.seqlens[b] = static_cast<int32_t>(p + 1);
+    a.rpos32[b] = static_cast<int32_t>(p + a.rope_off[b]);
+    chosen = nxt;
+  }
+  __syncthreads();
+  if (a.x == nullptr) return;
+  // fused embedding + first RMSNorm of the chosen token: 128 threads x D/128 elements
+  constexpr int PER = D / 128;
+  const int64_t t = chosen;
+  float v[PER];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    v[i] = __bfloat162float(a.emb[t * D + tid * PER + i]);
+    ss += v[i] * v[i];
+    a.x[static_cast<int64_t>(b) * D + tid * PER + i] = __float2bfloat16_rn(v[i]);
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) sred[warp] = ss;
+  __syncthreads();
+  ss = sred[0] + sred[1] + sred[2] + sred[3];
+  const float r = rsqrtf(ss / static_cast<float>(D) + a.eps);
+#pragma unroll
+  for (int i = 0; i < PER; ++i)
+    a.h[static_cast<int64_t>(b) * D + tid * PER + i] =
+        __float2bfloat16_rn(v[i] * r * __bfloat162float(a.norm_w[tid * PER + i]));
+  pdl_launch_dependents();
+}
+
+__global__ void cast_f32_bf16_kernel(const float* src, __nv_bfloat16* dst, int64_t n) {
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (i + 3 < n) {
+    const float4 v = *reinterpret_cast<const float4*>(src + i);
+    *reinterpret_cast<uint2*>(dst + i) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  } else {
+    for (int64_t k = i; k < n; ++k) dst[k] = __float2bfloat16_rn(src[k]);
+  }
+}
+
+// dst[i] = src[idx[i]] for rows of row_bytes (a multiple of 16).
+__global__ void gather_rows_kernel(const uint8_t* src, const int64_t* idx, uint8_t* dst, int64_t n, int row_bytes,
+                                   int64_t src_rows) {
+  const int64_t r = blockIdx.x;
+  pdl_wait();
+  if (r >= n) return;
+  const int64_t s = idx[r];
+  if (s < 0 || s >= src_rows) {
+    if (threadIdx.x == 0) raise_error(ERR_BOUNDS);
+    return;
+  }
+  for (int c = threadIdx.x * 16; c < row_bytes; c += blockDim.x * 16)
+    *reinterpret_cast<uint4*>(dst + r * row_bytes + c) = *reinterpret_cast<const uint4*>(src + s * row_bytes + c);
+}
+
+// dst[dst_idx[i]] = src[src_idx[i]] (either index may be null = identity).
+__global__ void copy_rows_kernel(const uint8_t* src, const int64_t* sidx, int64_t src_rows, uint8_t* dst,
+                                 const int64_t* didx, int64_t dst_rows, int64_t n, int row_bytes) {
+  const int64_t r = blockIdx.x;
+  pdl_wait();
+  if (r >= n) return;
+  const int64_t s = sidx ? sidx[r] : r;
+  const int64_t d = didx ? didx[r] : r;
+  if (s < 0 || s >= src_rows || d < 0 || d >= dst_rows) {
+    if (threadIdx.x == 0) raise_error(ERR_BOUNDS);
+    return;
+  }
+  for (int c = threadIdx.x * 16; c < row_bytes; c += blockDim.x * 16)
+    *reinterpret_cast<uint4*>(dst + d * row_bytes + c) = *reinterpret_cast<const uint4*>(src + s * row_bytes + c);
+}
+
+// x[rows[i]] = emb[token] (the BOS rows of the packed prefill, viktor/engine.py:165).
+__global__ void scatter_embed_kernel(__nv_bfloat16* x, const int64_t* rows, int64_t n, int64_t x_rows,
+                                     const __nv_bfloat16* emb, int64_t token, int D) {
+  const int64_t r = blockIdx.x;
+  pdl_wait();
+  if (r >= n) return;
+  const int64_t dr = rows[r];
+  if (dr < 0 || dr >= x_rows) {
+    if (threadIdx.x == 0) raise_error(ERR_BOUNDS);
+    return;
+  }
+  for (int c = threadIdx.x * 8; c < D; c += blockDim.x * 8)
+    *reinterpret_cast<uint4*>(x + dr * D + c) = *reinterpret_cast<const uint4*>(emb + token * D + c);
+}
+
+}  // namespace ew
+}  // namespace vk

@@ -1,0 +1,431 @@
+// C ABI of the viktor_b200 kernels (declared in include/viktor_b200.h).  Single translation unit: the kernel
+// headers are included here so that all kernels share one device error word without relocatable device code.
+#include <algorithm>
+#include <cstring>
+#include <utility>
+
+#include "decode_attention.cuh"
+#include "elementwise.cuh"
+#include "gemm_tc.cuh"
+#include "prefill_attention.cuh"
+#include "vk_host.cuh"
+
+namespace vk {
+
+static int g_pdl = 1;
+
+// Per-device record of kernels whose dynamic shared-memory limit has been raised.  The first launch of each
+// kernel on a device must happen outside stream capture (engines warm up eagerly before capturing).
+template <typename K>
+static bool ensure_smem(K kernel, int bytes) {
+  struct Entry {
+    const void* fn;
+    uint64_t mask;
+  };
+  static Entry table[64];
+  static int used = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const uint64_t bit = 1ull << (dev & 63);
+  const void* fn = reinterpret_cast<const void*>(kernel);
+  int i = 0;
+  for (; i < used; ++i)
+    if (table[i].fn == fn) break;
+  if (i < used && (table[i].mask & bit)) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  if (i == used) {
+    if (used == 64) return true;
+    table[used++] = Entry{fn, 0};
+  }
+  table[i].mask |= bit;
+  return true;
+}
+
+template <typename... KArgs, typename... Args>
+static int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void* stream, int cluster_x,
+                  Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attrs[2];
+  int na = 0;
+  if (g_pdl) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (cluster_x > 1) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = cluster_x;
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) {
+    fprintf(stderr, "viktor_b200: launch failed: %s\n", cudaGetErrorString(e));
+    return VK_ERR_CUDA;
+  }
+  return VK_OK;
+}
+
+static inline unsigned blocks_for(int64_t n, int per) { return static_cast<unsigned>((n + per - 1) / per); }
+
+// ---- GEMM dispatch ----------------------------------------------------------------------------------------
+template <int BN, int STAGES, int EPI>
+static int run_gemm(const void* A, const void* B, int64_t M, int N, int K, const gemm::EpiArgs& ep, int grid_x,
+                    int cluster_x, int64_t b_rows, void* stream) {
+  using L = gemm::Smem<BN, STAGES>;
+  if (M <= 0 || M > (int64_t(1) << 31) - 128) return VK_ERR_ARG;
+  if (K <= 0 || K % gemm::BK != 0) return VK_ERR_ARG;
+  if (!aligned16(A) || !aligned16(B)) return VK_ERR_ARG;
+  CUtensorMap ta, tb;
+  const uint32_t b_box = EPI == gemm::SWIGLU ? BN / 2 : BN;
+  if (!make_map_kmajor(&ta, A, static_cast<uint64_t>(M), K, K, gemm::BM)) return VK_ERR_ARG;
+  if (!make_map_kmajor(&tb, B, static_cast<uint64_t>(b_rows), K, K, b_box)) return VK_ERR_ARG;
+  auto kern = gemm::gemm_kernel<BN, STAGES, EPI>;
+  if (!ensure_smem(kern, L::TOTAL)) return VK_ERR_CUDA;
+  dim3 grid(grid_x, static_cast<unsigned>((M + gemm::BM - 1) / gemm::BM));
+  return launch(kern, grid, dim3(gemm::kThreads), L::TOTAL, stream, cluster_x, ta, tb, static_cast<int>(M), N, K,
+                ep);
+}
+
+static gemm::EpiArgs epi_zero() {
+  gemm::EpiArgs e;
+  memset(&e, 0, sizeof(e));
+  return e;
+}
+
+constexpr int64_t kSmallM = 4096;  // decode-sized GEMMs use narrow tiles (more CTAs), prefill wide tiles
+
+}  // namespace vk
+
+using namespace vk;
+
+extern "C" {
+
+int vk_version(void) { return 100; }
+
+int vk_read_device_errors(uint32_t* bits, int clear) {
+  if (!bits) return VK_ERR_ARG;
+  if (cudaMemcpyFromSymbol(bits, vk::g_error_word, sizeof(uint32_t)) != cudaSuccess) return VK_ERR_CUDA;
+  if (clear) {
+    const uint32_t z = 0;
+    if (cudaMemcpyToSymbol(vk::g_error_word, &z, sizeof(uint32_t)) != cudaSuccess) return VK_ERR_CUDA;
+  }
+  return VK_OK;
+}
+
+int vk_set_pdl(int enable) {
+  vk::g_pdl = enable ? 1 : 0;
+  return VK_OK;
+}
+
+int vk_add_rmsnorm(void* x, const void* delta, const void* w, void* h, int64_t n, int d, float eps, void* stream) {
+  if (n < 0 || d != 512 || !x || !w || !h) return n == 0 ? VK_OK : VK_ERR_ARG;
+  if (n == 0) return VK_OK;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(h) || (delta && !aligned16(delta))) return VK_ERR_ARG;
+  return launch(ew::rmsnorm_rows_kernel<512>, dim3(blocks_for(n, 8)), dim3(256), 0, stream, 1,
+                static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(delta),
+                static_cast<const int64_t*>(nullptr), static_cast<const __nv_bfloat16*>(nullptr), int64_t(0),
+                static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(h), n, eps);
+}
+
+int vk_embed_rmsnorm(const int64_t* tok, const void* emb, int64_t vocab, const void* w, void* x, void* h, int64_t n,
+                     int d, float eps, void* stream) {
+  if (n == 0) return VK_OK;
+  if (n < 0 || d != 512 || !tok || !emb || !w || !x || !h || vocab <= 0) return VK_ERR_ARG;
+  if (!aligned16(emb) || !aligned16(w) || !aligned16(x) || !aligned16(h)) return VK_ERR_ARG;
+  return launch(ew::rmsnorm_rows_kernel<512>, dim3(blocks_for(n, 8)), dim3(256), 0, stream, 1,
+                static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(nullptr), tok,
+                static_cast<const __nv_bfloat16*>(emb), vocab, static_cast<const __nv_bfloat16*>(w),
+                static_cast<__nv_bfloat16*>(h), n, eps);
+}
+
+int vk_qkv_rope_cache(const void* qkv, const void* q_norm_w, const void* k_norm_w, const float* cos,
+                      const float* sin, int rope_len, const int32_t* pos, const int32_t* rope_pos,
+                      const int32_t* seq, void* q, void* k_cache, void* v_cache, void* k_out, void* v_out,
+                      int64_t n, int64_t stride_cb, int64_t stride_cs, int cache_rows, int cache_len, float eps,
+                      int n_heads, int n_kv_heads, int head_dim, void* stream) {
+  if (n == 0) return VK_OK;
+  if (head_dim != 64 || n_heads <= 0 || n_kv_heads <= 0) return VK_ERR_UNSUPPORTED;
+  if (n < 0 || !qkv || !q_norm_w || !k_norm_w || !cos || !sin || !pos || !seq || !q || !k_cache || !v_cache)
+    return VK_ERR_ARG;
+  if (!aligned16(qkv) || !aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || stride_cs % 8 ||
+      stride_cb % 8 || (k_out && !aligned16(k_out)) || (v_out && !aligned16(v_out)))
+    return VK_ERR_ARG;
+  const int64_t threads = n * (n_heads + 2 * n_kv_heads);
+  return launch(ew::qkv_rope_cache_kernel, dim3(blocks_for(threads, 128)), dim3(128), 0, stream, 1,
+                static_cast<const __nv_bfloat16*>(qkv), static_cast<const __nv_bfloat16*>(q_norm_w),
+                static_cast<const __nv_bfloat16*>(k_norm_w), cos, sin, rope_len, pos, rope_pos, seq,
+                static_cast<__nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(k_cache),
+                static_cast<__nv_bfloat16*>(v_cache), static_cast<__nv_bfloat16*>(k_out),
+                static_cast<__nv_bfloat16*>(v_out), n, stride_cb, stride_cs, cache_rows, cache_len, eps, n_heads,
+                n_kv_heads);
+}
+
+int vk_linear(const void* x, const void* w, void* y, int64_t M, int N, int K, int swiglu, int out_f32,
+              void* stream) {
+  if (M == 0) return VK_OK;
+  if (!x || !w || !y || N <= 0 || M < 0) return VK_ERR_ARG;
+  gemm::EpiArgs ep = epi_zero();
+  ep.y = y;
+  if (swiglu) {
+    if (out_f32 || N % 2) return VK_ERR_ARG;
+    const int F = N / 2;
+    ep.ldy = F;
+    ep.n_valid = F;
+    if (M <= kSmallM) {
+      if (F % 32) return VK_ERR_ARG;
+      return run_gemm<64, 6, gemm::SWIGLU>(x, w, M, N, K, ep, F / 32, 1, N, stream);
+    }
+    if (F % 128) return VK_ERR_ARG;
+    return run_gemm<256, 4, gemm::SWIGLU>(x, w, M, N, K, ep, F / 128, 1, N, stream);
+  }
+  ep.ldy = N;
+  ep.n_valid = N;
+  if (out_f32) {
+    if (N <= 16) return run_gemm<16, 6, gemm::STORE_F32>(x, w, M, N, K, ep, 1, 1, N, stream);
+    if (N <= 64) return run_gemm<64, 6, gemm::STORE_F32>(x, w, M, N, K, ep, 1, 1, N, stream);
+    return run_gemm<128, 4, gemm::STORE_F32>(x, w, M, N, K, ep, (N + 127) / 128, 1, N, stream);
+  }
+  if (N <= 16) return run_gemm<16, 6, gemm::STORE_BF16>(x, w, M, N, K, ep, 1, 1, N, stream);
+  if (N <= 64 || M <= kSmallM)
+    return run_gemm<64, 6, gemm::STORE_BF16>(x, w, M, N, K, ep, (N + 63) / 64, 1, N, stream);
+  return run_gemm<128, 4, gemm::STORE_BF16>(x, w, M, N, K, ep, (N + 127) / 128, 1, N, stream);
+}
+
+int vk_swiglu(const void* gu, void* out, int64_t n, int F, void* stream) {
+  if (n == 0) return VK_OK;
+  if (!gu || !out || n < 0 || F <= 0) return VK_ERR_ARG;
+  return launch(ew::swiglu_kernel, dim3(blocks_for(n * F, 256)), dim3(256), 0, stream, 1,
+                static_cast<const __nv_bfloat16*>(gu), static_cast<__nv_bfloat16*>(out), n, F);
+}
+
+int vk_greedy_update(const float* logits, int64_t ld_logits, const float* bias, const uint8_t* is_tail,
+                     const uint8_t* is_homo, int homo_stop, int64_t* tok, int64_t* run, int64_t* pos,
+                     const int64_t* plen, const int64_t* rope_off, int64_t* out, int64_t out_stride,
+                     int64_t out_cols, int32_t* pos32, int32_t* seqlens, int32_t* rpos32, int B, int V, int eos,
+                     int pad, const void* emb, const void* norm_w, void* x, void* h, float eps, void* stream) {
+  if (B == 0) return VK_OK;
+  if (B < 0 || V <= 0 || !logits || !bias || !is_tail || !is_homo || !tok || !run || !pos || !plen || !rope_off ||
+      !out || !pos32 || !seqlens || !rpos32)
+    return VK_ERR_ARG;
+  if (emb && (!norm_w || !x || !h)) return VK_ERR_ARG;
+  ew::GreedyArgs a;
+  a.logits = logits;
+  a.ld_logits = ld_logits;
+  a.bias = bias;
+  a.is_tail = is_tail;
+  a.is_homo = is_homo;
+  a.homo_stop = homo_stop;
+  a.tok = tok;
+  a.run = run;
+  a.pos = pos;
+  a.plen = plen;
+  a.rope_off = rope_off;
+  a.out = out;
+  a.out_stride = out_stride;
+  a.out_cols = out_cols;
+  a.pos32 = pos32;
+  a.seqlens = seqlens;
+  a.rpos32 = rpos32;
+  a.B = B;
+  a.V = V;
+  a.eos = eos;
+  a.pad = pad;
+  a.emb = static_cast<const __nv_bfloat16*>(emb);
+  a.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
+  a.x = static_cast<__nv_bfloat16*>(emb ? x : nullptr);
+  a.h = static_cast<__nv_bfloat16*>(h);
+  a.eps = eps;
+  return launch(ew::greedy_kernel<512>, dim3(B), dim3(128), 0, stream, 1, a);
+}
+
+size_t vk_decode_attention_workspace_bytes(int nq, int S) {
+  if (nq <= 0 || S <= 0) return 0;
+  const size_t splits = (S + attn::kChunk - 1) / attn::kChunk;
+  const size_t counters = ((size_t)nq * 4 + 255) / 256 * 256;
+  const size_t ml = ((size_t)nq * splits * 8 * 2 * 4 + 255) / 256 * 256;
+  const size_t o = (size_t)nq * splits * 8 * 64 * 4;
+  return counters + ml + o;
+}
+
+static bool make_cache_maps(CUtensorMap* mk, CUtensorMap* mv, const void* k, const void* v, int cache_rows, int S,
+                            int64_t stride_kb, int64_t stride_ks) {
+  uint64_t dims[4] = {64, 2, static_cast<uint64_t>(S), static_cast<uint64_t>(cache_rows)};
+  uint64_t strides[3] = {128, static_cast<uint64_t>(stride_ks) * 2, static_cast<uint64_t>(stride_kb) * 2};
+  uint32_t box[4] = {64, 1, 64, 1};
+  return make_map_bf16(mk, k, 4, dims, strides, box, true) && make_map_bf16(mv, v, 4, dims, strides, box, true);
+}
+
+int vk_decode_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* lengths, void* out,
+                        int nq, int row0, int cache_rows, int S, int64_t stride_kb, int64_t stride_ks,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (nq == 0) return VK_OK;
+  if (nq < 0 || !q || !k_cache || !v_cache || !lengths || !out || !workspace || S <= 0 || row0 < 0 ||
+      row0 + nq > cache_rows || stride_ks < 128 || stride_kb < stride_ks * S)
+    return VK_ERR_ARG;
+  if (!aligned16(q) || !aligned16(out) || !aligned16(workspace)) return VK_ERR_ARG;
+  if (workspace_bytes < vk_decode_attention_workspace_bytes(nq, S)) return VK_ERR_ARG;
+  CUtensorMap mk, mv;
+  if (!make_cache_maps(&mk, &mv, k_cache, v_cache, cache_rows, S, stride_kb, stride_ks)) return VK_ERR_ARG;
+  const int splits = (S + attn::kChunk - 1) / attn::kChunk;
+  attn::DecodeArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.lengths = lengths;
+  a.row0 = row0;
+  a.nq = nq;
+  a.max_splits = splits;
+  a.S = S;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  a.counters = reinterpret_cast<int*>(ws);
+  const size_t counters = ((size_t)nq * 4 + 255) / 256 * 256;
+  a.ws_ml = reinterpret_cast<float*>(ws + counters);
+  a.ws_o = reinterpret_cast<float*>(ws + counters + ((size_t)nq * splits * 8 * 2 * 4 + 255) / 256 * 256);
+  a.scale_log2 = 0.125f * 1.4426950408889634f;
+  if (!ensure_smem(attn::decode_attn_kernel, attn::kSmemBytes)) return VK_ERR_CUDA;
+  return launch(attn::decode_attn_kernel, dim3(splits, nq), dim3(attn::kThreads), attn::kSmemBytes, stream, 1, mk,
+                mv, a);
+}
+
+int vk_prefill_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* cu_seqlens,
+                         int nseq, int max_seqlen, int64_t n_tok, int row0, int cache_rows, int S,
+                         int64_t stride_kb, int64_t stride_ks, void* out, void* stream) {
+  if (nseq == 0 || n_tok == 0) return VK_OK;
+  if (nseq < 0 || !q || !k_cache || !v_cache || !cu_seqlens || !out || max_seqlen <= 0 || max_seqlen > S ||
+      row0 < 0 || row0 + nseq > cache_rows || stride_ks < 128 || stride_kb < stride_ks * S)
+    return VK_ERR_ARG;
+  if (!aligned16(q) || !aligned16(out)) return VK_ERR_ARG;
+  CUtensorMap mq, mk, mv;
+  {
+    uint64_t dims[3] = {64, 8, static_cast<uint64_t>(n_tok)};
+    uint64_t strides[2] = {128, 1024};
+    uint32_t box[3] = {64, 1, 64};
+    if (!make_map_bf16(&mq, q, 3, dims, strides, box, true)) return VK_ERR_ARG;
+  }
+  if (!make_cache_maps(&mk, &mv, k_cache, v_cache, cache_rows, S, stride_kb, stride_ks)) return VK_ERR_ARG;
+  pattn::PrefillArgs a;
+  a.cu_seqlens = cu_seqlens;
+  a.nseq = nseq;
+  a.row0 = row0;
+  a.n_qtiles = (max_seqlen + 63) / 64;
+  a.S = S;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.scale_log2 = 0.125f * 1.4426950408889634f;
+  if (!ensure_smem(pattn::prefill_attn_kernel, pattn::kSmemBytes)) return VK_ERR_CUDA;
+  return launch(pattn::prefill_attn_kernel, dim3(a.n_qtiles, 8, nseq), dim3(pattn::kThreads), pattn::kSmemBytes,
+                stream, 1, mq, mk, mv, a);
+}
+
+int vk_linear_qkv_rope_cache(const void* h, const void* w_qkv, const void* q_norm_w, const void* k_norm_w,
+                             const float* cos, const float* sin, int rope_len, const int32_t* pos,
+                             const int32_t* rope_pos, const int32_t* seq, void* q, void* k_cache, void* v_cache,
+                             void* k_out, void* v_out, int64_t M, int64_t stride_cb, int64_t stride_cs,
+                             int cache_rows, int cache_len, float eps, int n_heads, int n_kv_heads,
+                             void* stream) {
+  if (M == 0) return VK_OK;
+  if (n_heads != 8 || n_kv_heads != 2) return VK_ERR_UNSUPPORTED;
+  if (M < 0 || !h || !w_qkv || !q_norm_w || !k_norm_w || !cos || !sin || !pos || !seq || !q || !k_cache ||
+      !v_cache)
+    return VK_ERR_ARG;
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || stride_cs % 8 || stride_cb % 8 ||
+      !aligned16(cos) || !aligned16(sin) || (k_out && !aligned16(k_out)) || (v_out && !aligned16(v_out)))
+    return VK_ERR_ARG;
+  gemm::EpiArgs ep = epi_zero();
+  ep.q_out = static_cast<__nv_bfloat16*>(q);
+  ep.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  ep.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  ep.k_out = static_cast<__nv_bfloat16*>(k_out);
+  ep.v_out = static_cast<__nv_bfloat16*>(v_out);
+  ep.pos = pos;
+  ep.rope_pos = rope_pos;
+  ep.seq = seq;
+  ep.q_norm_w = static_cast<const __nv_bfloat16*>(q_norm_w);
+  ep.k_norm_w = static_cast<const __nv_bfloat16*>(k_norm_w);
+  ep.cos = cos;
+  ep.sin = sin;
+  ep.rope_len = rope_len;
+  ep.cache_rows = cache_rows;
+  ep.cache_len = cache_len;
+  ep.stride_cb = stride_cb;
+  ep.stride_cs = stride_cs;
+  ep.n_heads = n_heads;
+  ep.n_kv_heads = n_kv_heads;
+  ep.eps = eps;
+  const int N = (n_heads + 2 * n_kv_heads) * 64;
+  if (M <= kSmallM) return run_gemm<64, 6, gemm::QKV_ROPE>(h, w_qkv, M, N, 512, ep, N / 64, 1, N, stream);
+  return run_gemm<256, 4, gemm::QKV_ROPE>(h, w_qkv, M, N, 512, ep, N / 256, 1, N, stream);
+}
+
+int vk_linear_add_rmsnorm(const void* a, const void* w, void* x, const void* norm_w, void* h, int64_t M, int K,
+                          float eps, void* stream) {
+  if (M == 0) return VK_OK;
+  if (M < 0 || !a || !w || !x || !norm_w || !h) return VK_ERR_ARG;
+  if (!aligned16(x) || !aligned16(h)) return VK_ERR_ARG;
+  gemm::EpiArgs ep = epi_zero();
+  ep.x = static_cast<__nv_bfloat16*>(x);
+  ep.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
+  ep.h_out = static_cast<__nv_bfloat16*>(h);
+  ep.eps = eps;
+  if (M <= kSmallM) return run_gemm<64, 6, gemm::ADD_RMSNORM>(a, w, M, 512, K, ep, 8, 8, 512, stream);
+  return run_gemm<256, 4, gemm::ADD_RMSNORM>(a, w, M, 512, K, ep, 2, 2, 512, stream);
+}
+
+int vk_linear_bias_act(const void* x, const void* w, const void* bias, void* y, int64_t ldy, const int32_t* row_map,
+                       int64_t M, int N, int K, int act, void* stream) {
+  if (M == 0) return VK_OK;
+  if (M < 0 || !x || !w || !bias || !y || N <= 0 || N % 16 || ldy < N || (act != 0 && act != 1)) return VK_ERR_ARG;
+  gemm::EpiArgs ep = epi_zero();
+  ep.y = y;
+  ep.ldy = ldy;
+  ep.n_valid = N;
+  ep.row_map = row_map;
+  ep.bias = static_cast<const __nv_bfloat16*>(bias);
+  ep.act = act;
+  if (M <= kSmallM)
+    return run_gemm<64, 6, gemm::BIAS_ACT>(x, w, M, N, K, ep, (N + 63) / 64, 1, N, stream);
+  return run_gemm<128, 4, gemm::BIAS_ACT>(x, w, M, N, K, ep, (N + 127) / 128, 1, N, stream);
+}
+
+int vk_cast_f32_bf16(const float* src, void* dst, int64_t n, void* stream) {
+  if (n == 0) return VK_OK;
+  if (!src || !dst || n < 0 || !aligned16(src) || (reinterpret_cast<uintptr_t>(dst) & 7)) return VK_ERR_ARG;
+  return launch(ew::cast_f32_bf16_kernel, dim3(blocks_for((n + 3) / 4, 256)), dim3(256), 0, stream, 1, src,
+                static_cast<__nv_bfloat16*>(dst), n);
+}
+
+int vk_gather_rows(const void* src, const int64_t* idx, void* dst, int64_t n, int row_bytes, int64_t src_rows,
+                   void* stream) {
+  if (n == 0) return VK_OK;
+  if (!src || !idx || !dst || n < 0 || row_bytes <= 0 || row_bytes % 16 || !aligned16(src) || !aligned16(dst))
+    return VK_ERR_ARG;
+  return launch(ew::gather_rows_kernel, dim3(static_cast<unsigned>(n)), dim3(128), 0, stream, 1,
+                static_cast<const uint8_t*>(src), idx, static_cast<uint8_t*>(dst), n, row_bytes, src_rows);
+}
+
+int vk_copy_rows(const void* src, const int64_t* src_idx, int64_t src_rows, void* dst, const int64_t* dst_idx,
+                 int64_t dst_rows, int64_t n, int row_bytes, void* stream) {
+  if (n == 0) return VK_OK;
+  if (!src || !dst || n < 0 || row_bytes <= 0 || row_bytes % 16 || !aligned16(src) || !aligned16(dst))
+    return VK_ERR_ARG;
+  return launch(ew::copy_rows_kernel, dim3(static_cast<unsigned>(n)), dim3(128), 0, stream, 1,
+                static_cast<const uint8_t*>(src), src_idx, src_rows, static_cast<uint8_t*>(dst), dst_idx, dst_rows, n,
+                row_bytes);
+}
+
+int vk_scatter_embed(void* x, const int64_t* rows, int64_t n, int64_t x_rows, const void* emb, int64_t token, int d,
+                     void* stream) {
+  if (n == 0) return VK_OK;
+  if (!x || !rows || !emb || n < 0 || d <= 0 || d % 8 || !aligned16(x) || !aligned16(emb) || token < 0)
+    return VK_ERR_ARG;
+  return launch(ew::scatter_embed_kernel, dim3(static_cast<unsigned>(n)), dim3(64), 0, stream, 1,
+                static_cast<__nv_bfloat16*>(x), rows, n, x_rows, static_cast<const __nv_bfloat16*>(emb), token, d);
+}
+
+}  // extern "C"

@@ -1,0 +1,139 @@
+"""Inference forward of the decoder on the B200 kernels (the role of viktor/fast_decoder.py).
+
+Tokens are packed [n_tokens, d]: prefill packs the prefixes of many variable-length chunks (cu_seqlens), a
+decode step is one token per sequence.  Per layer (viktor/fast_decoder.py:33-60), with the reference's
+separate ops fused into tensor-core GEMM epilogues:
+
+    q, K/V -> cache  = linear_qkv_rope_cache(h)        (linear + qkv_rope_cache)
+    o                = attention(q, cache)             (prefill: varlen causal; decode / BOS-only: split-K)
+    x += o W_o, h    = linear_add_rmsnorm(o)            (linear + add_rmsnorm)
+    g                = linear(h, gate_up, swiglu)       (linear with SwiGLU epilogue)
+    x += g W_down, h = linear_add_rmsnorm(g)            (linear + add_rmsnorm with the next norm's weight)
+
+The prefill runs the last layer for the BOS rows only (viktor/fast_decoder.py:48-53): all K/V are kept, the
+final signal outputs have no consumer.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ._lib import call
+from .decoder import rope_tables
+
+_BF16 = torch.bfloat16
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+class DeviceWeights:
+    """bf16 device copies of the projector + decoder weights, in the layouts the kernels read."""
+
+    def __init__(self, model, device):
+        dec = model.decoder
+        cfg = dec.cfg
+        if (cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim) != (512, 8, 2, 64):
+            raise NotImplementedError("the kernels are built for d_model 512, 8 query / 2 KV heads, head_dim 64")
+        if cfg.ffn_dim % 128:
+            raise NotImplementedError("ffn_dim must be a multiple of 128")
+
+        def w(t):
+            return t.detach().to(device=device, dtype=_BF16).contiguous()
+
+        self.cfg = cfg
+        self.eps = float(cfg.norm_eps)
+        self.embed = w(dec.embed.weight)
+        self.vocab = cfg.vocab_size
+        # lm_head rows padded to a multiple of 16 (tensor-core N granularity); padded logits are never read
+        vpad = -(-cfg.vocab_size // 16) * 16
+        head = torch.zeros(vpad, cfg.d_model, dtype=_BF16, device=device)
+        head[:cfg.vocab_size] = w(dec.lm_head.weight)
+        self.lm_head, self.vpad = head, vpad
+        self.norm = w(dec.norm.weight)
+        self.layers = []
+        for blk in dec.layers:
+            a = blk.attn
+            self.layers.append(dict(attn_norm=w(blk.attn_norm.weight), qkv=w(a.qkv_proj.weight),
+                                    q_norm=w(a.q_norm.weight), k_norm=w(a.k_norm.weight), o=w(a.o_proj.weight),
+                                    mlp_norm=w(blk.mlp_norm.weight), gate_up=w(blk.gate_up.weight),
+                                    down=w(blk.down.weight)))
+        cos, sin = rope_tables(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta)
+        self.cos, self.sin = cos.to(device).contiguous(), sin.to(device).contiguous()
+        proj = model.projector
+        self.proj = (w(proj[0].weight), w(proj[0].bias), w(proj[2].weight), w(proj[2].bias))
+        self.d_enc = proj[0].weight.shape[1]
+        if self.d_enc % 64:
+            raise NotImplementedError("encoder width must be a multiple of 64")
+
+    def next_norm(self, i):
+        return self.layers[i + 1]["attn_norm"] if i + 1 < len(self.layers) else self.norm
+
+
+class FastDecoder:
+    """Layer loop over the fused kernels.  All buffers are passed in; nothing is allocated per call except
+    where noted."""
+
+    def __init__(self, weights: DeviceWeights):
+        self.w = weights
+        self.cfg = weights.cfg
+
+    # -- helpers -----------------------------------------------------------------------------------------------
+    def _qkv(self, i, h, pos, seq, rope_pos, cache, q_out, stream):
+        L = self.w.layers[i]
+        kc, vc = cache.k[i], cache.v[i]
+        call("vk_linear_qkv_rope_cache", _p(h), _p(L["qkv"]), _p(L["q_norm"]), _p(L["k_norm"]), _p(self.w.cos),
+             _p(self.w.sin), self.w.cos.shape[0], _p(pos), _p(rope_pos), _p(seq), _p(q_out), _p(kc), _p(vc), None,
+             None, h.shape[0], kc.stride(0), kc.stride(1), kc.shape[0], kc.shape[1], self.w.eps, 8, 2, stream)
+
+    def _decode_attn(self, i, q, lengths, cache, out, workspace, row0, stream):
+        kc, vc = cache.k[i], cache.v[i]
+        call("vk_decode_attention", _p(q), _p(kc), _p(vc), _p(lengths), _p(out), q.shape[0], row0, kc.shape[0],
+             kc.shape[1], kc.stride(0), kc.stride(1), _p(workspace), workspace.numel(), stream)
+
+    def _mlp_tail(self, i, o, x, h, g, stream):
+        """x += o W_o; h = norm(x); g = swiglu(h W_gu); x += g W_d; h = next_norm(x)."""
+        L = self.w.layers[i]
+        M = x.shape[0]
+        call("vk_linear_add_rmsnorm", _p(o), _p(L["o"]), _p(x), _p(L["mlp_norm"]), _p(h), M, 512, self.w.eps, stream)
+        call("vk_linear", _p(h), _p(L["gate_up"]), _p(g), M, L["gate_up"].shape[0], 512, 1, 0, stream)
+        call("vk_linear_add_rmsnorm", _p(g), _p(L["down"]), _p(x), _p(self.w.next_norm(i)), _p(h), M, g.shape[1],
+             self.w.eps, stream)
+
+    # -- prefill -----------------------------------------------------------------------------------------------
+    def prefill(self, x, h, pos, seq, cu_seqlens, max_seqlen, cache, q, o, g, row0=0, rope_pos=None,
+                last_indices=None, lengths=None, x_last=None, h_last=None, q_last=None, o_last=None, g_last=None,
+                workspace=None, stream=None):
+        """x [n, d] packed prefix embeddings (residual stream, updated in place); h its first attention norm.
+        pos/seq [n] int32; cu_seqlens [b+1] int32.  Fills the cache rows row0.. of those sequences.  Returns the
+        final-normed hidden of every row (h), or with last_indices [b] int64 (+ lengths [b] int32 = T_b and the
+        *_last buffers) only that of each sequence's last row (h_last)."""
+        stream = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
+        n_layers = self.cfg.n_layers
+        n = x.shape[0]
+        for i in range(n_layers):
+            self._qkv(i, h, pos, seq, rope_pos, cache, q, stream)
+            kc, vc = cache.k[i], cache.v[i]
+            if last_indices is not None and i == n_layers - 1:
+                b = last_indices.shape[0]
+                call("vk_gather_rows", _p(x), _p(last_indices), _p(x_last), b, 1024, n, stream)
+                call("vk_gather_rows", _p(q), _p(last_indices), _p(q_last), b, 1024, n, stream)
+                self._decode_attn(i, q_last, lengths, cache, o_last, workspace, row0, stream)
+                self._mlp_tail(i, o_last, x_last, h_last, g_last, stream)
+                return h_last
+            call("vk_prefill_attention", _p(q), _p(kc), _p(vc), _p(cu_seqlens), cu_seqlens.shape[0] - 1,
+                 int(max_seqlen), n, row0, kc.shape[0], kc.shape[1], kc.stride(0), kc.stride(1), _p(o), stream)
+            self._mlp_tail(i, o, x, h, g, stream)
+        return h
+
+    # -- one decode step -----------------------------------------------------------------------------------------
+    def decode(self, x, h, pos32, rows, seqlens, cache, q, o, g, workspace, rope_pos=None, stream=None):
+        """One token per sequence: x [B, d] residual, h its first attention norm (from the previous step's
+        greedy kernel); pos32/rows [B] int32; seqlens = pos + 1.  Returns the final-normed hidden h [B, d]."""
+        stream = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
+        for i in range(self.cfg.n_layers):
+            self._qkv(i, h, pos32, rows, rope_pos, cache, q, stream)
+            self._decode_attn(i, q, seqlens, cache, o, workspace, 0, stream)
+            self._mlp_tail(i, o, x, h, g, stream)
+        return h
