@@ -78,9 +78,10 @@ def test_linear_swiglu(M):
     gu = (x.float() @ w.float().T).to(BF)
     g, u = gu.float().chunk(2, -1)
     ref = F.silu(g) * u
-    assert (y.float() - ref).abs().max() < 0.05
+    # outputs reach |8| here, where one bf16 ulp is 0.03: compare relative to the output range
+    assert (y.float() - ref).abs().max() / ref.abs().max() < 1e-2
     # the unfused op agrees with the fused epilogue
-    assert (swiglu(gu).float() - ref).abs().max() < 0.05
+    assert (swiglu(gu).float() - ref).abs().max() / ref.abs().max() < 1e-2
 
 
 @pytest.mark.parametrize("M,K", [(3, 512), (256, 512), (256, 1536), (1000, 1536), (5000, 512)])
