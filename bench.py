@@ -1,0 +1,352 @@
+"""Benchmark of the Viktor decoder hot path on B200: decoded bases/s and microseconds per decode step.
+
+One bench step = one ``DecodeEngine.generate`` over a batch of chunks (packed prefill of the projected frames,
+then a fixed number of greedy CUDA-graph decode steps with EOS masked, so every step emits one token per
+chunk).  Default workload: 256 chunks x 2048 frames x 512 features ~ N(0, 1), 1100
+decode steps, single-base vocabulary (7), 8-layer d512 GQA 8/2 decoder with N(0, 0.02) random weights, bf16.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4]
+
+Multi-GPU: one process per GPU under torch.distributed.run; every rank runs its own engine on its own chunks
+(weak scaling, no collective on the data path); the barrier / max-over-ranks timing uses NCCL.
+
+Printed keys beyond the base contract:
+  roofline      decode attention (the dominant kernel): algorithmic KV bytes per launch / measured launch time
+  cpu_baseline  the reference path on the host cores (PyTorch CPU fp32 port) on a bounded sample, rank 0, N=1
+  e2e           the same metric through the public API from pinned host frames, tokens copied back each step
+  decode_us_per_step, prefill_ms_per_chunk, gpu_launches, clocks
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    2: dict(name="config2: 256 chunks x 2048 frames, 1100 greedy steps, vocab 7", B=256, frames="full", steps=1100,
+            k=1),
+    3: dict(name="config3: 512 chunks x U{128..2048 step 128} frames, 1100 greedy steps, vocab 7", B=512,
+            frames="varlen", steps=1100, k=1),
+    4: dict(name="config4: 1024 chunks x 2048 frames, 280 greedy steps, 4-mer vocab 343", B=1024, frames="full",
+            steps=280, k=4),
+}
+PLEN = 2048
+HBM_FALLBACK_GBS = 6650.0
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return HBM_FALLBACK_GBS, "fallback"
+
+
+def ncu_traffic_ratio():
+    """DRAM bytes / algorithmic bytes of one decode-attention launch, from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "decode_attention_config2.md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("traffic_over_algorithmic:"):
+            return float(line.split(":")[1])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples taken while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_lens(cfg, B, seed):
+    from viktor_b200.synthetic import varlen_prefix_lengths
+    return [PLEN] * B if cfg["frames"] == "full" else varlen_prefix_lengths(B, seed=seed)
+
+
+def cpu_baseline(args, cfg):
+    """The reference path on the host cores: a multithreaded PyTorch-CPU fp32 restatement (oracle/decoder_torch.py,
+    pinned to the reference's golden tokens) on a bounded sample of the same workload: 4 chunks x 2048 frames,
+    prefill + the workload's full number of greedy steps."""
+    import torch
+    from oracle import OracleConfig
+    from oracle.decoder_torch import TorchCPUModel
+    from viktor_b200.config import DecoderConfig
+    from viktor_b200.synthetic import make_frames, make_weights
+    B = 4
+    steps = args.cpu_steps or cfg["steps"]
+    V = 7 if cfg["k"] == 1 else 343
+    dc = DecoderConfig(vocab_size=V, rope_theta=1e6)
+    tm = TorchCPUModel(OracleConfig(vocab_size=V, rope_theta=1e6), make_weights(dc, seed=0, init="normal"),
+                       k=cfg["k"])
+    lens = [PLEN] * B
+    frames = make_frames(lens, seed=1)
+    bias = np.zeros(V, np.float32)
+    bias[[0, 1, 2]] = -np.inf
+    t0 = time.perf_counter()
+    out = tm.generate(frames, lens, steps, bias, None)
+    dt = time.perf_counter() - t0
+    bases = int(tm.tok.n_bases[out].sum())
+    return {"value": bases / dt, "unit": "bases/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{B} chunks x {PLEN} frames, prefill + {steps} greedy steps, PyTorch CPU fp32 restatement "
+                      f"of the reference path ({dt:.1f} s)"}
+
+
+def run_reference_arm(args, cfg, rank):
+    if rank != 0:
+        return
+    res = [cpu_baseline(args, cfg) for _ in range(max(1, args.steps))]
+    vals = [r["value"] for r in res]
+    v = statistics.median(vals)
+    line = {"metric": "decoded bases/s", "value": v, "unit": "bases/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": cfg["name"], "sample": res[0]["sample"]},
+            "cpu_baseline": dict(res[0], value=v),
+            "e2e": {"value": v, "unit": "bases/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def attention_roofline(eng, torch, lens, steps):
+    """Average launch time of the decode attention kernel at the mean decode length of the run, timed with
+    CUDA events on the launching stream; algorithmic bytes = K and V rows read + q read + o written."""
+    from viktor_b200._lib import call
+    B = eng.B
+    mid = torch.tensor([n + 1 + steps // 2 for n in lens], dtype=torch.int32, device=eng.device)
+    st = torch.cuda.current_stream(eng.device)
+    reps = 5
+    kc, vc = eng.cache.k, eng.cache.v
+
+    def launch(i):
+        call("vk_decode_attention", eng.q.data_ptr(), kc[i].data_ptr(), vc[i].data_ptr(), mid.data_ptr(),
+             eng.o.data_ptr(), B, 0, kc.shape[1], kc.shape[2], kc[i].stride(0), kc[i].stride(1),
+             eng.attn_ws.data_ptr(), eng.attn_ws.numel(), st.cuda_stream)
+
+    for i in range(8):
+        launch(i)
+    torch.cuda.synchronize(eng.device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        for i in range(8):
+            launch(i)
+    e1.record(st)
+    torch.cuda.synchronize(eng.device)
+    t = e0.elapsed_time(e1) / 1e3 / (reps * 8)
+    nbytes = int(mid.long().sum().item()) * 512 + B * 1024 * 2
+    return nbytes, t
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
+    ap.add_argument("--decode-steps", type=int, default=None, help="override the workload's decode steps")
+    ap.add_argument("--cpu-steps", type=int, default=None, help="CPU-baseline decode steps (default: workload's)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    cfg = dict(CONFIGS[args.config])
+    if args.decode_steps:
+        cfg["steps"] = args.decode_steps
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, cfg, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+
+    from viktor_b200 import Basecaller, DecodeEngine, DecoderConfig
+    from viktor_b200 import _lib
+    from viktor_b200.synthetic import make_weights
+
+    B, steps = cfg["B"], cfg["steps"]
+    V = 7 if cfg["k"] == 1 else 343
+    dcfg = DecoderConfig(vocab_size=V, rope_theta=1e6)
+    model = Basecaller.from_weights(make_weights(dcfg, seed=0, init="normal"), k=cfg["k"], cfg=dcfg)
+    lens = make_lens(cfg, B, seed=100 + rank)
+    eng = DecodeEngine(model, B, steps, PLEN, max_homopolymer=None, device=dev)
+    eng.bias[2] = float("-inf")  # EOS masked: fixed-length decode, every step emits a base
+    n_bases = torch.as_tensor(model.tokenizer.n_bases, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1 + rank)
+    frames = torch.randn(sum(lens), 512, generator=g, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    st = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        eng.generate(frames, lens, steps)
+    eng.check_errors()
+
+    # ---- device-resident timed region ----
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    bases = torch.zeros((), dtype=torch.long, device=dev)
+    launches0 = _lib.launches
+    barrier()
+    with ClockSampler(local) as clk:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(st)
+        for e0, e1, e2 in ev:
+            e0.record(st)
+            eng.prefill(frames, lens)
+            e1.record(st)
+            out = eng.decode(steps)
+            e2.record(st)
+            bases += n_bases[out].sum()
+        t_end.record(st)
+        barrier()
+    launches = _lib.launches - launches0
+    elapsed = t_start.elapsed_time(t_end) / 1e3
+    prefill_s = sum(a.elapsed_time(b) for a, b, _ in ev) / 1e3
+    decode_s = sum(b.elapsed_time(c) for _, b, c in ev) / 1e3
+    bases_rank = int(bases.item())
+    eng.check_errors()
+    if world > 1:
+        t = torch.tensor([elapsed, decode_s, prefill_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed, decode_s, prefill_s = t.tolist()
+        b = torch.tensor([bases_rank], device=dev, dtype=torch.long)
+        dist.all_reduce(b)
+        total_bases = int(b.item())
+    else:
+        total_bases = bases_rank
+    value = total_bases / elapsed
+
+    # ---- end to end through the public API: pinned host frames in, tokens back to the host ----
+    e2e = None
+    if not args.no_e2e:
+        host_frames = frames.cpu().pin_memory()
+        host_out = torch.empty(eng.out.shape, dtype=eng.out.dtype).pin_memory()
+        eng.generate(host_frames, lens, steps)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        hb = 0
+        for _ in range(args.steps):
+            out = eng.generate(host_frames, lens, steps)
+            host_out.copy_(out, non_blocking=True)
+            st.synchronize()
+            hb += int(model.tokenizer.n_bases[host_out.numpy()].sum())
+        e1.record(st)
+        barrier()
+        t_e2e = e0.elapsed_time(e1) / 1e3
+        if world > 1:
+            t = torch.tensor([t_e2e], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t_e2e = t.item()
+            b = torch.tensor([hb], device=dev, dtype=torch.long)
+            dist.all_reduce(b)
+            hb = int(b.item())
+        e2e = {"value": hb / t_e2e, "unit": "bases/s", "h2d_bytes_per_step": host_frames.numel() * 4,
+               "d2h_bytes_per_step": host_out.numel() * 8}
+
+    nbytes, t_attn = attention_roofline(eng, torch, lens, steps)
+    peak, peak_kind = peaks()
+    achieved = nbytes / t_attn / 1e9
+    ratio = ncu_traffic_ratio()
+    roofline = {"bound": "hbm", "kernel": "decode_attn_kernel", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                if peak_kind == "measured" else "fallback 6.65 TB/s",
+                "bytes_per_launch": nbytes, "launch_us": t_attn * 1e6,
+                "traffic": None if ratio is None else nbytes * ratio}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args, cfg)
+
+    if rank == 0:
+        line = {"metric": "decoded bases/s", "value": value, "unit": "bases/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": cfg["name"], "global_batch": B * world, "seq_len": PLEN + 1 + steps,
+                           "parallelism": f"dp{world} (independent chunk shards)",
+                           "l2": "inputs larger than L2 (KV cache 2 x 8 x B x 3149 x 256 B = 3.3 GB per GPU)"},
+                "decode_us_per_step": decode_s / (args.steps * (steps - 1)) * 1e6,
+                "prefill_ms_per_chunk": prefill_s / (args.steps * B) * 1e3,
+                "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -77,13 +77,14 @@ int vk_swiglu(const void* gu, void* out, int64_t n, int F, void* stream);
 /* viktor/triton_ops.py:200-209 greedy_update (+ viktor/engine.py:79-89 _select at temperature 0).
  * logits [B, V] f32 (row stride ld_logits); bias [V] f32; is_tail, is_homo [V] u8; tok, run, pos, plen,
  * rope_off [B] i64; out [B, out_cols] i64 (row stride out_stride); pos32, seqlens, rpos32 [B] i32.
- * When emb != NULL, additionally writes x = emb[new tok] and h = RMSNorm(x) * norm_w ([B, 512] bf16) for
- * the next decode step (the embed_rmsnorm of viktor/fast_decoder.py:80-81, fused). */
+ * When emb != NULL, additionally writes the next decode step's input: x = emb[new tok] ([B, 512] bf16) and its
+ * per-64-column sums of squares ssq ([B, 8] f32), which the first layer's folded RMSNorm consumes (the
+ * embed_rmsnorm of viktor/fast_decoder.py:80-81, fused). */
 int vk_greedy_update(const float* logits, int64_t ld_logits, const float* bias, const uint8_t* is_tail,
                      const uint8_t* is_homo, int homo_stop, int64_t* tok, int64_t* run, int64_t* pos,
                      const int64_t* plen, const int64_t* rope_off, int64_t* out, int64_t out_stride,
                      int64_t out_cols, int32_t* pos32, int32_t* seqlens, int32_t* rpos32, int B, int V, int eos,
-                     int pad, const void* emb, const void* norm_w, void* x, void* h, float eps, void* stream);
+                     int pad, const void* emb, void* x, float* ssq, void* stream);
 
 /* ---- attention: viktor/decode_attention.py, flash_attn calls of viktor/fast_decoder.py ------------------- */
 
@@ -107,27 +108,53 @@ int vk_prefill_attention(const void* q, const void* k_cache, const void* v_cache
                          int nseq, int max_seqlen, int64_t n_tok, int row0, int cache_rows, int S,
                          int64_t stride_kb, int64_t stride_ks, void* out, void* stream);
 
-/* ---- tensor-core projections with fused epilogues (the B200 forms of viktor/fast_decoder.py:33-60) ------- */
+/* ---- tensor-core projections with fused epilogues (the B200 forms of viktor/fast_decoder.py:33-60) -------
+ *
+ * Folded RMSNorm.  The decoder's pre-norm GEMMs compute (RMSNorm(x) * w) . W^T.  Here they run on the residual x
+ * itself with w folded into W's columns once (W' = bf16(W * w), vk_fold_norm_weight), and the epilogue scales row
+ * i by rsqrt(sum(ssq[i, 0..7]) / 512 + eps).  ssq [M, 8] f32 holds the sums of squares of the eight 64-column
+ * blocks of each 512-wide row of x; vk_linear_residual, vk_row_ssq and the fused greedy step produce it. */
 
-/* h [M, 512] bf16 . w_qkv [(H + 2 Hkv) * 64, 512]^T followed by the qkv_rope_cache epilogue (arguments as in
- * vk_qkv_rope_cache).  Replaces linear + qkv_rope_cache of viktor/fast_decoder.py:44-47. */
-int vk_linear_qkv_rope_cache(const void* h, const void* w_qkv, const void* q_norm_w, const void* k_norm_w,
-                             const float* cos, const float* sin, int rope_len, const int32_t* pos,
-                             const int32_t* rope_pos, const int32_t* seq, void* q, void* k_cache, void* v_cache,
-                             void* k_out, void* v_out, int64_t M, int64_t stride_cb, int64_t stride_cs,
-                             int cache_rows, int cache_len, float eps, int n_heads, int n_kv_heads,
-                             void* stream);
+/* (RMSNorm(x) * w) . W^T with W' = W diag(w) given (w_folded): x [M, 512] bf16, ssq [M, 8] f32.  Output as in
+ * vk_linear (swiglu / out_f32).  Replaces add_rmsnorm's h followed by linear (viktor/fast_decoder.py:56,
+ * viktor/engine.py:96). */
+int vk_linear_rmsnorm(const void* x, const float* ssq, float eps, const void* w_folded, void* y, int64_t M, int N,
+                      int K, int swiglu, int out_f32, void* stream);
 
-/* a [M, K] bf16 . w [512, K]^T = delta, then x += delta (bf16, in place) and h = RMSNorm(x) * norm_w
- * ([M, 512] bf16).  Replaces mm + add_rmsnorm of viktor/fast_decoder.py:55,57-59.  K a multiple of 64. */
-int vk_linear_add_rmsnorm(const void* a, const void* w, void* x, const void* norm_w, void* h, int64_t M, int K,
-                          float eps, void* stream);
+/* q, K/V <- (RMSNorm(x) * w_attn) . W_qkv^T followed by the qkv_rope_cache epilogue (arguments as in
+ * vk_qkv_rope_cache; eps is the QK-norm epsilon).  ssq NULL: x is used as given (w_qkv not folded).
+ * Replaces add_rmsnorm + linear + qkv_rope_cache of viktor/fast_decoder.py:41-47. */
+int vk_linear_qkv_rope_cache(const void* x, const float* ssq, float norm_eps, const void* w_qkv,
+                             const void* q_norm_w, const void* k_norm_w, const float* cos, const float* sin,
+                             int rope_len, const int32_t* pos, const int32_t* rope_pos, const int32_t* seq, void* q,
+                             void* k_cache, void* v_cache, void* k_out, void* v_out, int64_t M, int64_t stride_cb,
+                             int64_t stride_cs, int cache_rows, int cache_len, float eps, int n_heads,
+                             int n_kv_heads, void* stream);
 
-/* y = act(x [M, K] . w [N, K]^T + bias) as bf16; act 0 = identity, 1 = GELU (erf).  Row i of the result goes
- * to row row_map[i] of y (row_map NULL = identity; ldy = row stride of y).  The projector of
+/* x += bf16(a [M, K] . w [512, K]^T) in place (bf16), and ssq_out [M, 8] f32 = sums of squares of the new rows'
+ * 64-column blocks.  The residual half of linear + add_rmsnorm (viktor/fast_decoder.py:55,57-59). */
+int vk_linear_residual(const void* a, const void* w, void* x, float* ssq_out, int64_t M, int K, void* stream);
+
+/* viktor/fast_decoder.py:55,57-59 as one call: x += a . w^T (bf16) and h = RMSNorm(x) * norm_w ([M, 512] bf16).
+ * ssq_scratch [M, 8] f32 receives the row sums of squares.  K a multiple of 64. */
+int vk_linear_add_rmsnorm(const void* a, const void* w, void* x, const void* norm_w, void* h, float* ssq_scratch,
+                          int64_t M, int K, float eps, void* stream);
+
+/* y = act(x [M, K] . w [N, K]^T + bias) as bf16; act 0 = identity, 1 = GELU (erf); N a multiple of 64.  Row i of
+ * the result goes to row row_map[i] of y (row_map NULL = identity; ldy = row stride of y).  The projector of
  * viktor/model.py:35 and the packed-prefill scatter of viktor/engine.py:163-164. */
 int vk_linear_bias_act(const void* x, const void* w, const void* bias, void* y, int64_t ldy,
                        const int32_t* row_map, int64_t M, int N, int K, int act, void* stream);
+
+/* ssq [n, 8] f32 = sums of squares of the eight 64-column blocks of each row of x [n, 512] bf16. */
+int vk_row_ssq(const void* x, float* ssq, int64_t n, int d, void* stream);
+
+/* h = bf16(x * rsqrt(sum(ssq[row]) / 512 + eps) * w): RMSNorm from precomputed sums of squares. */
+int vk_ssq_rmsnorm(const void* x, const float* ssq, const void* w, void* h, int64_t n, int d, float eps,
+                   void* stream);
+
+/* out [N, K] bf16 = bf16(w [N, K] * norm_w [K]): folds an RMSNorm weight into the GEMM that consumes it. */
+int vk_fold_norm_weight(const void* w, const void* norm_w, void* out, int64_t N, int K, void* stream);
 
 /* ---- layout helpers --------------------------------------------------------------------------------------- */
 int vk_cast_f32_bf16(const float* src, void* dst, int64_t n, void* stream);

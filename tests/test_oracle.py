@@ -48,3 +48,16 @@ def test_tokenizer_matches_reference_layout():
             assert not any(tok.tail_mask[i] for i in ids[:-1])
             assert tok.decode(ids + [EOS, 5]) == s
             assert int(tok.n_bases[ids].sum()) == n
+
+
+@pytest.mark.parametrize("name", ["base_theta1e6", "kmer4", "homopolymer", "base_b8"])
+def test_torch_cpu_baseline_port_matches_reference(name):
+    """The port timed as the CPU baseline produces the reference's greedy tokens."""
+    from oracle.decoder_torch import TorchCPUModel
+    g = load(name)
+    m = g["meta"]
+    if m["pos_scale"] != 1:
+        pytest.skip("the timed port covers pos_scale 1")
+    tm = TorchCPUModel(OracleConfig(**m["cfg"]), g["weights"], k=m["k"])
+    out = tm.generate(g["frames"], m["lens"], m["max_new"], g["bias"], m["max_homopolymer"])
+    np.testing.assert_array_equal(out, g["tokens"])

@@ -28,13 +28,18 @@ _SIGS = {
     "vk_linear": (i32, [p, p, p, i64, i32, i32, i32, i32, p]),
     "vk_swiglu": (i32, [p, p, i64, i32, p]),
     "vk_greedy_update": (i32, [p, i64, p, p, p, i32, p, p, p, p, p, p, i64, i64, p, p, p, i32, i32, i32, i32, p, p,
-                               p, p, f32, p]),
+                               p, p]),
     "vk_decode_attention_workspace_bytes": (sz, [i32, i32]),
     "vk_decode_attention": (i32, [p, p, p, p, p, i32, i32, i32, i32, i64, i64, p, sz, p]),
     "vk_prefill_attention": (i32, [p, p, p, p, i32, i32, i64, i32, i32, i32, i64, i64, p, p]),
-    "vk_linear_qkv_rope_cache": (i32, [p, p, p, p, p, p, i32, p, p, p, p, p, p, p, p, i64, i64, i64, i32, i32, f32,
-                                       i32, i32, p]),
-    "vk_linear_add_rmsnorm": (i32, [p, p, p, p, p, i64, i32, f32, p]),
+    "vk_linear_rmsnorm": (i32, [p, p, f32, p, p, i64, i32, i32, i32, i32, p]),
+    "vk_linear_qkv_rope_cache": (i32, [p, p, f32, p, p, p, p, p, i32, p, p, p, p, p, p, p, p, i64, i64, i64, i32, i32,
+                                       f32, i32, i32, p]),
+    "vk_linear_residual": (i32, [p, p, p, p, i64, i32, p]),
+    "vk_linear_add_rmsnorm": (i32, [p, p, p, p, p, p, i64, i32, f32, p]),
+    "vk_row_ssq": (i32, [p, p, i64, i32, p]),
+    "vk_ssq_rmsnorm": (i32, [p, p, p, p, i64, i32, f32, p]),
+    "vk_fold_norm_weight": (i32, [p, p, p, i64, i32, p]),
     "vk_linear_bias_act": (i32, [p, p, p, p, i64, p, i64, i32, i32, i32, p]),
     "vk_cast_f32_bf16": (i32, [p, p, i64, p]),
     "vk_gather_rows": (i32, [p, p, p, i64, i32, i64, p]),
@@ -43,6 +48,8 @@ _SIGS = {
 }
 
 _lib = None
+_HOST_ONLY = {"vk_version", "vk_read_device_errors", "vk_set_pdl", "vk_decode_attention_workspace_bytes"}
+launches = 0  # kernels launched through call() (each launching entry point launches exactly one kernel)
 
 
 def lib_path() -> str:
@@ -70,9 +77,12 @@ def exported_symbols() -> list[str]:
 
 def call(name: str, *args):
     """Calls an entry point and raises RuntimeError on a non-zero status."""
+    global launches
     rc = getattr(load(), name)(*args)
     if rc != VK_OK:
         raise RuntimeError(f"{name} failed: {_STATUS.get(rc, rc)}")
+    if name not in _HOST_ONLY:
+        launches += 1
     return rc
 
 

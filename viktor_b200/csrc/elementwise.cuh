@@ -9,6 +9,12 @@
 namespace vk {
 namespace ew {
 
+VK_DEV void load8(const __nv_bfloat16* src, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(src);
+  v[0] = bf16_lo(u.x); v[1] = bf16_hi(u.x); v[2] = bf16_lo(u.y); v[3] = bf16_hi(u.y);
+  v[4] = bf16_lo(u.z); v[5] = bf16_hi(u.z); v[6] = bf16_lo(u.w); v[7] = bf16_hi(u.w);
+}
+
 VK_DEV float warp_sum(float v) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -180,12 +186,10 @@ struct GreedyArgs {
   int32_t* seqlens;
   int32_t* rpos32;
   int B, V, eos, pad;
-  // optional fused embedding of the chosen token
+  // optional fused embedding of the chosen token: x = emb[tok] and its per-64-column sums of squares
   const __nv_bfloat16* emb;
-  const __nv_bfloat16* norm_w;
   __nv_bfloat16* x;
-  __nv_bfloat16* h;
-  float eps;
+  float* ssq;
 };
 
 template <int D>
@@ -193,7 +197,6 @@ __global__ void __launch_bounds__(128) greedy_kernel(GreedyArgs a) {
   __shared__ float sv[4];
   __shared__ int si[4];
   __shared__ int64_t chosen;
-  __shared__ float sred[4];
   const int b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_wait();
@@ -256,27 +259,75 @@ __global__ void __launch_bounds__(128) greedy_kernel(GreedyArgs a) {
   }
   __syncthreads();
   if (a.x == nullptr) return;
-  // fused embedding + first RMSNorm of the chosen token: 128 threads x D/128 elements
+  // fused embedding of the chosen token for the next step: x = emb[tok] and the sums of squares of its eight
+  // 64-column blocks (consumed by the folded attention norm of layer 0)
   constexpr int PER = D / 128;
   const int64_t t = chosen;
-  float v[PER];
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
-    v[i] = __bfloat162float(a.emb[t * D + tid * PER + i]);
-    ss += v[i] * v[i];
-    a.x[static_cast<int64_t>(b) * D + tid * PER + i] = __float2bfloat16_rn(v[i]);
+    const __nv_bfloat16 v = a.emb[t * D + tid * PER + i];
+    const float f = __bfloat162float(v);
+    ss += f * f;
+    a.x[static_cast<int64_t>(b) * D + tid * PER + i] = v;
   }
-  ss = warp_sum(ss);
-  if (lane == 0) sred[warp] = ss;
-  __syncthreads();
-  ss = sred[0] + sred[1] + sred[2] + sred[3];
-  const float r = rsqrtf(ss / static_cast<float>(D) + a.eps);
+  // 64 columns = 16 threads (PER = 4): reduce over groups of 16 lanes
 #pragma unroll
-  for (int i = 0; i < PER; ++i)
-    a.h[static_cast<int64_t>(b) * D + tid * PER + i] =
-        __float2bfloat16_rn(v[i] * r * __bfloat162float(a.norm_w[tid * PER + i]));
+  for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((tid & 15) == 0) a.ssq[static_cast<int64_t>(b) * 8 + tid / 16] = ss;
   pdl_launch_dependents();
+}
+
+// Per-row sums of squares of the eight 64-column blocks of x [n, 512] (bf16), one warp per row.
+__global__ void __launch_bounds__(256) row_ssq_kernel(const __nv_bfloat16* x, float* ssq, int64_t n) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  pdl_wait();
+  if (row >= n) return;
+  // lane holds columns [16*lane, 16*lane + 16): four lanes per 64-column block
+  float v[16];
+  load8(x + row * 512 + lane * 16, v);
+  load8(x + row * 512 + lane * 16 + 8, v + 8);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) ss += v[i] * v[i];
+  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+  if ((lane & 3) == 0) ssq[row * 8 + lane / 4] = ss;
+  pdl_launch_dependents();
+}
+
+// h = bf16(x * rsqrt(sum(ssq[row]) / 512 + eps) * w), 8 elements per thread.
+__global__ void ssq_rmsnorm_kernel(const __nv_bfloat16* x, const float* ssq, const __nv_bfloat16* w,
+                                   __nv_bfloat16* h, int64_t n, float eps) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  pdl_wait();
+  if (i >= n * 64) return;
+  const int64_t row = i / 64;
+  const int c = static_cast<int>(i % 64) * 8;
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) s += ssq[row * 8 + k];
+  const float r = rsqrtf(s / 512.f + eps);
+  float v[8], wv[8], o[8];
+  load8(x + row * 512 + c, v);
+  load8(w + c, wv);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) o[k] = v[k] * r * wv[k];
+  uint4 u;
+  u.x = pack_bf16x2(o[0], o[1]);
+  u.y = pack_bf16x2(o[2], o[3]);
+  u.z = pack_bf16x2(o[4], o[5]);
+  u.w = pack_bf16x2(o[6], o[7]);
+  *reinterpret_cast<uint4*>(h + row * 512 + c) = u;
+}
+
+// out[n][k] = bf16(w[n][k] * norm_w[k]) (product of two bf16 values in fp32, rounded once).
+__global__ void fold_norm_kernel(const __nv_bfloat16* w, const __nv_bfloat16* nw, __nv_bfloat16* out, int64_t N,
+                                 int K) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= N * K) return;
+  out[i] = __float2bfloat16_rn(__bfloat162float(w[i]) * __bfloat162float(nw[i % K]));
 }
 
 __global__ void cast_f32_bf16_kernel(const float* src, __nv_bfloat16* dst, int64_t n) {

@@ -1,22 +1,31 @@
 // tcgen05 GEMM for the decoder projections:  C[M, N] = A[M, K] * B[N, K]^T  (bf16 in, fp32 accumulate in TMEM).
 //
-// One CTA computes one 128 x BN tile.  Warp roles (192 threads):
-//   warp 0      TMA producer (one elected lane): A and B K-major tiles, 128-byte swizzle, STAGES-deep ring
+// One CTA computes one 128 x BN tile over a K range.  Warp roles (192 threads):
+//   warp 0      TMA producer (one elected lane): A and B K-major tiles, 128-byte swizzle, up to 4-deep ring
 //   warp 1      TMEM allocator + MMA issuer (one elected lane): tcgen05.mma kind::f16, M=128, N=BN, K=16 x 4
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (thread = one output row = one TMEM lane), then the
-//               fused epilogue writes the result straight to global memory.
+//   warps 2..5  epilogue (thread = one accumulator row = one TMEM lane)
 //
-// Fused epilogues (each restates a reference op on the GEMM output, see the per-epilogue comments):
-//   STORE_BF16 / STORE_F32   plain y = acc (viktor/triton_ops.py:111-146 without SwiGLU; fp32 logits)
-//   BIAS_ACT                 y = act(bf16(acc + bias)), act = identity | GELU(erf); optional output row map
-//                            (projector, viktor/model.py:35, and the packed-prefill scatter, viktor/engine.py:163-165)
-//   SWIGLU                   B rows = [gate block | up block]: y = bf16(bf16(silu(bf16 g)) * bf16 u)
+// Split-K across a thread-block cluster (NK > 1): the NK CTAs of a cluster share one output tile and each
+// accumulates K/NK of the contraction.  Partial tiles are staged in shared memory and reduced on chip through
+// distributed shared memory: CTA k sums rows [k*128/NK, (k+1)*128/NK) over all NK peers and runs the epilogue on
+// them.  Small-M (decode) GEMMs thereby spread over 100-200 CTAs that each stream only 24-72 KB, instead of a few
+// CTAs streaming hundreds of KB.
+//
+// Folded RMSNorm: a GEMM whose input is RMSNorm(x) * w runs on x itself with w folded into the weight columns
+// (W' = W diag(w), done once when the weights are loaded); the epilogue scales each row by
+// r = rsqrt(mean(x^2) + eps), with mean(x^2) assembled from the per-64-column sums of squares (ssq) that the
+// producer of x wrote.  That keeps every epilogue tile-local.
+//
+// Fused epilogues (each restates a reference op on the GEMM output):
+//   STORE_BF16 / STORE_F32   y = r * acc (viktor/triton_ops.py:111-146 without SwiGLU; fp32 logits)
+//   BIAS_ACT                 y = act(bf16(acc + bias)), act = identity | GELU(erf), optional output row map
+//                            (projector, viktor/model.py:35; packed-prefill scatter, viktor/engine.py:163-165)
+//   SWIGLU                   B rows = [gate block | up block]: y = bf16(bf16(silu(bf16(r g))) * bf16(r u))
 //                            (viktor/triton_ops.py:129-134, :212-220)
-//   QKV_ROPE                 per 64-column head: QK-RMSNorm, RoPE, q store, K/V cache write
+//   QKV_ROPE                 per 64-column head of bf16(r * acc): QK-RMSNorm, RoPE, q store, K/V cache write
 //                            (viktor/triton_ops.py:43-91)
-//   ADD_RMSNORM              x += bf16(acc) in place; h = bf16(x * rsqrt(mean(x^2) + eps) * w).  The row spans
-//                            the N/BN CTAs of a thread-block cluster; per-row partial sums of squares are
-//                            exchanged through distributed shared memory (viktor/triton_ops.py:17-31)
+//   ADD_RESID                x = bf16(x + bf16(acc)) in place and the new row's per-64-column sums of squares
+//                            (the residual half of viktor/triton_ops.py:17-31; the norm half is folded forward)
 #pragma once
 
 #include "vk_common.cuh"
@@ -27,49 +36,59 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
+constexpr int kMaxStages = 4;
+constexpr int kSsqSlots = 8;  // sums of squares per 512-wide residual row, one per 64-column block
 
-enum Epi : int { STORE_BF16 = 0, STORE_F32 = 1, BIAS_ACT = 2, SWIGLU = 3, QKV_ROPE = 4, ADD_RMSNORM = 5 };
+enum Epi : int { STORE_BF16 = 0, STORE_F32 = 1, BIAS_ACT = 2, SWIGLU = 3, QKV_ROPE = 4, ADD_RESID = 5 };
 
 struct EpiArgs {
-  // STORE_*, BIAS_ACT, SWIGLU
   void* y;
   int64_t ldy;
-  int n_valid;                     // output columns that exist (STORE_*: <= N)
+  int n_valid;                     // output columns that exist (STORE_*, BIAS_ACT)
   const int32_t* row_map;          // BIAS_ACT: output row of each input row (nullptr = identity)
   const __nv_bfloat16* bias;       // BIAS_ACT
   int act;                         // BIAS_ACT: 0 identity, 1 GELU(erf)
+  const float* ssq_in;             // folded RMSNorm of A: [M, 8] sums of squares (nullptr = no norm)
+  float eps;
   // QKV_ROPE
   __nv_bfloat16* q_out;            // [M, H, 64]
-  __nv_bfloat16* k_cache;          // one layer: [rows, S, Hkv, 64] with the strides below
+  __nv_bfloat16* k_cache;          // one layer: element (row, p, kvh, d) at row*stride_cb + p*stride_cs + kvh*64 + d
   __nv_bfloat16* v_cache;
   __nv_bfloat16* k_out;            // optional packed [M, Hkv, 64]
   __nv_bfloat16* v_out;
   const int32_t* pos;              // cache position of each token
-  const int32_t* rope_pos;         // RoPE position of each token
+  const int32_t* rope_pos;         // RoPE position of each token (nullptr = pos)
   const int32_t* seq;              // cache row of each token
   const __nv_bfloat16* q_norm_w;   // [64]
   const __nv_bfloat16* k_norm_w;   // [64]
   const float* cos;                // [rope_len, 32]
   const float* sin;
   int rope_len;
-  int cache_rows, cache_len;       // bounds of the cache (rows, positions)
-  int64_t stride_cb, stride_cs;    // cache strides in elements
+  int cache_rows, cache_len;
+  int64_t stride_cb, stride_cs;
   int n_heads, n_kv_heads;
-  float eps;
-  // ADD_RMSNORM
-  __nv_bfloat16* x;                // residual [M, N], updated in place
-  const __nv_bfloat16* norm_w;     // [N]
-  __nv_bfloat16* h_out;            // [M, N]
+  float qk_eps;
+  // ADD_RESID
+  __nv_bfloat16* x;                // residual [M, 512], updated in place
+  float* ssq_out;                  // [M, 8]
 };
 
-template <int BN, int STAGES>
-struct Smem {
-  static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
-  static constexpr int RED_OFF = BAR_OFF + 256;
-  static constexpr int TOTAL = RED_OFF + BM * 4 + 1024;  // + alignment slack
+// Shared-memory layout (bytes from the 1024-aligned base), identical in every CTA of a launch.
+struct SmemLayout {
+  int stages, stage_bytes, a_bytes, red_off, bar_off, total;
+  __host__ __device__ SmemLayout(int bn, int nk, int stages_) {
+    stages = stages_;
+    a_bytes = BM * BK * 2;
+    stage_bytes = a_bytes + bn * BK * 2;
+    int pipe = stages * stage_bytes;
+    const int staging = nk > 1 ? BM * (bn + 4) * 4 : 0;
+    if (staging > pipe) pipe = staging;
+    pipe = (pipe + 1023) & ~1023;
+    red_off = pipe;
+    const int red = nk > 1 ? (BM / nk) * (bn + 4) * 4 : 0;
+    bar_off = (red_off + red + 15) & ~15;
+    total = bar_off + 128 + 1024;  // barriers + alignment slack
+  }
 };
 
 __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
@@ -95,6 +114,15 @@ VK_DEV void load_bf16x8(const __nv_bfloat16* src, float* v) {
 VK_DEV float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
 VK_DEV float silu(float g) { return g * (1.0f / (1.0f + __expf(-g))); }
 
+// Row scale of a folded RMSNorm: rsqrt(mean(x^2) + eps) from the producer's eight partial sums.
+VK_DEV float row_rscale(const EpiArgs& ep, int row) {
+  if (!ep.ssq_in) return 1.f;
+  const float4* p = reinterpret_cast<const float4*>(ep.ssq_in + static_cast<int64_t>(row) * kSsqSlots);
+  const float4 a = p[0], b = p[1];
+  const float s = ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w));
+  return rsqrtf(s * (1.0f / 512.0f) + ep.eps);
+}
+
 // QK-RMSNorm + RoPE of one 64-wide head held by this thread (viktor/triton_ops.py:44-49).
 VK_DEV void norm_rope_head(float* v, const __nv_bfloat16* w, const float* c, const float* s, float eps) {
   float ss = 0.f;
@@ -110,32 +138,165 @@ VK_DEV void norm_rope_head(float* v, const __nv_bfloat16* w, const float* c, con
   }
 }
 
-template <int BN, int STAGES, int EPI>
+// Number of epilogue chunks of a BN tile and their width.  A chunk is 64 consecutive columns (BN < 64: BN
+// columns); for SWIGLU it is 32 gate columns and the 32 matching up columns.
+template <int BN>
+struct Chunks {
+  static constexpr int W = BN < 64 ? BN : 64;
+  static constexpr int COUNT = BN < 64 ? 1 : BN / 64;
+};
+
+// Applies the epilogue to chunk `ch` of row `row` (v holds W values; SWIGLU: 32 gate then 32 up).
+template <int BN, int EPI>
+VK_DEV void epi_chunk(const EpiArgs& ep, int row, int n_tile, int ch, float* v, float r, int N) {
+  constexpr int W = Chunks<BN>::W;
+  if (EPI == STORE_BF16 || EPI == STORE_F32 || EPI == BIAS_ACT) {
+    const int col = n_tile * BN + ch * W;
+    const int64_t orow = (EPI == BIAS_ACT && ep.row_map) ? ep.row_map[row] : row;
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
+      if (EPI == BIAS_ACT) {
+        const float t = bf16_round(v[i] + (col + i < ep.n_valid ? __bfloat162float(ep.bias[col + i]) : 0.f));
+        v[i] = ep.act == 1 ? gelu_erf(t) : t;
+      } else {
+        v[i] *= r;
+      }
+    }
+    if (EPI == STORE_F32) {
+      float* yp = reinterpret_cast<float*>(ep.y) + orow * ep.ldy + col;
+      if (col + W <= ep.n_valid && (ep.ldy & 3) == 0) {
+#pragma unroll
+        for (int i = 0; i < W; i += 4)
+          *reinterpret_cast<float4*>(yp + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      } else {
+        for (int i = 0; i < W; ++i)
+          if (col + i < ep.n_valid) yp[i] = v[i];
+      }
+    } else {
+      __nv_bfloat16* yp = reinterpret_cast<__nv_bfloat16*>(ep.y) + orow * ep.ldy + col;
+      if (col + W <= ep.n_valid && (ep.ldy & 7) == 0) {
+#pragma unroll
+        for (int i = 0; i < W; i += 8) store_bf16x8(yp + i, v + i);
+      } else {
+        for (int i = 0; i < W; ++i)
+          if (col + i < ep.n_valid) yp[i] = __float2bfloat16_rn(v[i]);
+      }
+    }
+  } else if (EPI == SWIGLU) {
+    const int F = N / 2;
+    const int o0 = n_tile * (BN / 2) + ch * 32;
+    float out[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float gb = bf16_round(v[i] * r);
+      out[i] = bf16_round(silu(gb)) * bf16_round(v[32 + i] * r);
+    }
+    if (o0 + 32 <= F) {
+      __nv_bfloat16* yp = reinterpret_cast<__nv_bfloat16*>(ep.y) + static_cast<int64_t>(row) * ep.ldy + o0;
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) store_bf16x8(yp + i, out + i);
+    }
+  } else if (EPI == ADD_RESID) {
+    const int c0 = n_tile * BN + ch * 64;
+    __nv_bfloat16* xp = ep.x + static_cast<int64_t>(row) * N + c0;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; i += 8) {
+      float xo[8];
+      load_bf16x8(xp + i, xo);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        xo[e] = bf16_round(xo[e] + bf16_round(v[i + e]));
+        ss += xo[e] * xo[e];
+      }
+      store_bf16x8(xp + i, xo);
+    }
+    ep.ssq_out[static_cast<int64_t>(row) * kSsqSlots + c0 / 64] = ss;
+  } else if (EPI == QKV_ROPE) {
+    const int H = ep.n_heads, HKV = ep.n_kv_heads;
+    const int gh = n_tile * (BN / 64) + ch;
+    const int p = ep.pos[row];
+    const int rp = ep.rope_pos ? ep.rope_pos[row] : p;
+    const int sq = ep.seq[row];
+    if (p < 0 || p >= ep.cache_len || sq < 0 || sq >= ep.cache_rows || rp < 0 || rp >= ep.rope_len) {
+      raise_error(ERR_BOUNDS);
+      return;
+    }
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = bf16_round(v[i] * r);  // the qkv linear output is stored in bf16
+    if (gh < H + HKV) {
+      float c[32], s[32];
+      const float4* cp = reinterpret_cast<const float4*>(ep.cos + static_cast<int64_t>(rp) * 32);
+      const float4* sp = reinterpret_cast<const float4*>(ep.sin + static_cast<int64_t>(rp) * 32);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 a = cp[i], b = sp[i];
+        c[4 * i] = a.x; c[4 * i + 1] = a.y; c[4 * i + 2] = a.z; c[4 * i + 3] = a.w;
+        s[4 * i] = b.x; s[4 * i + 1] = b.y; s[4 * i + 2] = b.z; s[4 * i + 3] = b.w;
+      }
+      norm_rope_head(v, gh < H ? ep.q_norm_w : ep.k_norm_w, c, s, ep.qk_eps);
+    }
+    if (gh < H) {
+      __nv_bfloat16* qp = ep.q_out + (static_cast<int64_t>(row) * H + gh) * 64;
+#pragma unroll
+      for (int i = 0; i < 64; i += 8) store_bf16x8(qp + i, v + i);
+    } else if (gh < H + 2 * HKV) {
+      const bool is_k = gh < H + HKV;
+      const int kvh = is_k ? gh - H : gh - H - HKV;
+      __nv_bfloat16* cache = is_k ? ep.k_cache : ep.v_cache;
+      __nv_bfloat16* dst =
+          cache + static_cast<int64_t>(sq) * ep.stride_cb + static_cast<int64_t>(p) * ep.stride_cs + kvh * 64;
+#pragma unroll
+      for (int i = 0; i < 64; i += 8) store_bf16x8(dst + i, v + i);
+      __nv_bfloat16* packed = is_k ? ep.k_out : ep.v_out;
+      if (packed) {
+        __nv_bfloat16* pd = packed + (static_cast<int64_t>(row) * HKV + kvh) * 64;
+#pragma unroll
+        for (int i = 0; i < 64; i += 8) store_bf16x8(pd + i, v + i);
+      }
+    }
+  }
+}
+
+// TMEM column of element i of chunk ch (SWIGLU chunks gather gate and up halves).
+template <int BN, int EPI>
+VK_DEV int chunk_col(int ch, int i) {
+  constexpr int W = Chunks<BN>::W;
+  if (EPI == SWIGLU) return i < 32 ? ch * 32 + i : BN / 2 + ch * 32 + (i - 32);
+  return ch * W + i;
+}
+
+template <int BN, int EPI, int NK>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                int K, EpiArgs ep) {
-  using L = Smem<BN, STAGES>;
+                int K, int stages, EpiArgs ep) {
+  const SmemLayout L(BN, NK, stages);
+  constexpr int B_BOX_BYTES = (EPI == SWIGLU ? BN / 2 : BN) * BK * 2;
+  constexpr int SROW = BN + 4;   // staging row stride (floats)
+  constexpr int R = BM / NK;     // rows each CTA reduces
+  constexpr uint32_t TMEM_COLS = tmem_cols_for(BN);
+  constexpr int W = Chunks<BN>::W;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
-  uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* accum = empty + kMaxStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* red = reinterpret_cast<float*>(smem + L::RED_OFF);
-  constexpr uint32_t TMEM_COLS = tmem_cols_for(BN);
+  float* staging = reinterpret_cast<float*>(smem);
+  float* red = reinterpret_cast<float*>(smem + L.red_off);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_tile = blockIdx.x, m0 = blockIdx.y * BM;
-  const int num_kb = K / BK;
+  const int ks = NK > 1 ? static_cast<int>(blockIdx.x) : 0;
+  const int n_tile = blockIdx.y, m0 = blockIdx.z * BM;
+  const int nkb = K / BK / NK;
+  const int kb0 = ks * nkb;
 
   if (warp == 0 && lane == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum, 1);
-    *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -149,40 +310,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  bool ok = true;  // producer / MMA lanes: false once a wait ran out
   if (warp == 0) {
     if (lane == 0) {
-      // Weights do not depend on the previous kernel: start them before waiting on it.
-      const int pre = num_kb < STAGES ? num_kb : STAGES;
-      for (int kb = 0; kb < pre; ++kb) {
-        uint8_t* sB = smem + kb * L::STAGE_BYTES + L::A_BYTES;
-        mbar_expect_tx(&full[kb], L::STAGE_BYTES);
+      // The B operand (weights) does not depend on the previous kernel: start it before waiting on it.
+      const int pre = nkb < stages ? nkb : stages;
+      for (int i = 0; i < pre; ++i) {
+        uint8_t* sB = smem + i * L.stage_bytes + L.a_bytes;
+        const int kx = (kb0 + i) * BK;
+        mbar_expect_tx(&full[i], L.stage_bytes);
         if (EPI == SWIGLU) {
-          tma_load_2d(sB, &tmB, &full[kb], kb * BK, n_tile * (BN / 2));
-          tma_load_2d(sB + L::B_BYTES / 2, &tmB, &full[kb], kb * BK, N / 2 + n_tile * (BN / 2));
+          tma_load_2d(sB, &tmB, &full[i], kx, n_tile * (BN / 2));
+          tma_load_2d(sB + B_BOX_BYTES, &tmB, &full[i], kx, N / 2 + n_tile * (BN / 2));
         } else {
-          tma_load_2d(sB, &tmB, &full[kb], kb * BK, n_tile * BN);
+          tma_load_2d(sB, &tmB, &full[i], kx, n_tile * BN);
         }
       }
       pdl_wait();
-      for (int kb = 0; kb < pre; ++kb) tma_load_2d(smem + kb * L::STAGE_BYTES, &tmA, &full[kb], kb * BK, m0);
-      for (int kb = pre; kb < num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (*abort_flag) break;
+      for (int i = 0; i < pre; ++i) tma_load_2d(smem + i * L.stage_bytes, &tmA, &full[i], (kb0 + i) * BK, m0);
+      for (int i = pre; i < nkb; ++i) {
+        const int s = i % stages;
+        const uint32_t ph = (i / stages) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1)) {
           raise_error(ERR_WAIT_EMPTY);
-          *abort_flag = 1;
+          ok = false;
           break;
         }
-        uint8_t* sA = smem + s * L::STAGE_BYTES;
-        uint8_t* sB = sA + L::A_BYTES;
-        mbar_expect_tx(&full[s], L::STAGE_BYTES);
-        tma_load_2d(sA, &tmA, &full[s], kb * BK, m0);
+        uint8_t* sA = smem + s * L.stage_bytes;
+        uint8_t* sB = sA + L.a_bytes;
+        const int kx = (kb0 + i) * BK;
+        mbar_expect_tx(&full[s], L.stage_bytes);
+        tma_load_2d(sA, &tmA, &full[s], kx, m0);
         if (EPI == SWIGLU) {
-          tma_load_2d(sB, &tmB, &full[s], kb * BK, n_tile * (BN / 2));
-          tma_load_2d(sB + L::B_BYTES / 2, &tmB, &full[s], kb * BK, N / 2 + n_tile * (BN / 2));
+          tma_load_2d(sB, &tmB, &full[s], kx, n_tile * (BN / 2));
+          tma_load_2d(sB + B_BOX_BYTES, &tmB, &full[s], kx, N / 2 + n_tile * (BN / 2));
         } else {
-          tma_load_2d(sB, &tmB, &full[s], kb * BK, n_tile * BN);
+          tma_load_2d(sB, &tmB, &full[s], kx, n_tile * BN);
         }
       }
     } else {
@@ -192,210 +355,105 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
-      bool ok = true;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % stages;
+        const uint32_t ph = (i / stages) & 1;
         if (!mbar_wait(&full[s], ph)) {
           raise_error(ERR_WAIT_FULL);
-          *abort_flag = 1;
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint64_t ad = sdesc_k_sw128(smem_u32(smem + s * L::STAGE_BYTES));
-        const uint64_t bd = sdesc_k_sw128(smem_u32(smem + s * L::STAGE_BYTES + L::A_BYTES));
+        const uint64_t ad = sdesc_k_sw128(smem_u32(smem + s * L.stage_bytes));
+        const uint64_t bd = sdesc_k_sw128(smem_u32(smem + s * L.stage_bytes + L.a_bytes));
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k) umma_bf16(tmem_base, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+        for (int k = 0; k < BK / 16; ++k) umma_bf16(tmem_base, ad + 2 * k, bd + 2 * k, idesc, (i | k) != 0);
         umma_commit(&empty[s]);
       }
       if (ok) umma_commit(accum);
     }
-    __syncwarp();
   } else {
     pdl_wait();
   }
-
-  // ---------------- epilogue (warps 2..5) ----------------
-  // tcgen05.ld is warp-collective: every lane of an epilogue warp issues the same loads; only the global
-  // stores are predicated on the row being inside M.
   __syncwarp();
+
+  // ---------------- epilogue ----------------
+  // tcgen05.ld is warp-collective: every lane of an epilogue warp issues the same loads; only global stores
+  // depend on the row being inside M.
   const bool epi_warp = warp >= 2;
   const int quarter = warp & 3;
   const int row_local = quarter * 32 + lane;
-  const int row = m0 + row_local;
-  const bool row_ok = row < M;
   const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
   bool have_acc = false;
   if (epi_warp) {
     have_acc = __all_sync(0xffffffffu, mbar_wait(accum, 0));
-    if (!have_acc && lane == 0) {
-      raise_error(ERR_WAIT_ACCUM);
-      *abort_flag = 1;
-    }
+    if (!have_acc && lane == 0) raise_error(ERR_WAIT_ACCUM);
     tc_fence_after();
   }
   pdl_launch_dependents();
 
-  if (EPI == ADD_RMSNORM) {
-    // Phase 1: x_new = bf16(x + bf16(acc)) over this CTA's BN columns; partial sum of squares.
-    const int n0 = n_tile * BN;
+  if (NK == 1) {
     if (epi_warp && have_acc) {
-      float ss = 0.f;
+      const int row = m0 + row_local;
+      const bool row_ok = row < M;
+      const float r = (row_ok && EPI != BIAS_ACT && EPI != ADD_RESID) ? row_rscale(ep, row) : 1.f;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        float v[16];
-        tmem_ld16(taddr + c, v);
-        tmem_wait_ld();
-        if (row_ok) {
-          __nv_bfloat16* xp = ep.x + static_cast<int64_t>(row) * N + n0 + c;
-          float xo[16];
-          load_bf16x8(xp, xo);
-          load_bf16x8(xp + 8, xo + 8);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            xo[i] = bf16_round(xo[i] + bf16_round(v[i]));
-            ss += xo[i] * xo[i];
-          }
-          store_bf16x8(xp, xo);
-          store_bf16x8(xp + 8, xo + 8);
-        }
-      }
-      red[row_local] = ss;
-    }
-    cluster_sync();
-    // Phase 2: full-row sum of squares from every CTA of the cluster, then h = bf16(x * r * w).
-    if (epi_warp && have_acc && row_ok) {
-      const uint32_t cs = static_cast<uint32_t>(N / BN);
-      float tot = 0.f;
-      for (uint32_t r = 0; r < cs; ++r) tot += ld_dsmem_f32(&red[row_local], r);
-      const float rr = rsqrtf(tot / static_cast<float>(N) + ep.eps);
-      const __nv_bfloat16* xp = ep.x + static_cast<int64_t>(row) * N + n0;
-      __nv_bfloat16* hp = ep.h_out + static_cast<int64_t>(row) * N + n0;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 8) {
-        float xv[8], hv[8];
-        load_bf16x8(xp + c, xv);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) hv[i] = xv[i] * rr * __bfloat162float(ep.norm_w[n0 + c + i]);
-        store_bf16x8(hp + c, hv);
-      }
-    }
-    cluster_sync();
-  } else if (epi_warp && have_acc) {
-    if (EPI == STORE_BF16 || EPI == STORE_F32 || EPI == BIAS_ACT) {
-      const int n0 = n_tile * BN;
-      const int64_t orow = (EPI == BIAS_ACT && ep.row_map && row_ok) ? ep.row_map[row] : row;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        float v[16];
-        tmem_ld16(taddr + c, v);
-        tmem_wait_ld();
-        if (!row_ok) continue;
-        const int col = n0 + c;
-        if (EPI == BIAS_ACT) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float t = bf16_round(v[i] + (col + i < ep.n_valid ? __bfloat162float(ep.bias[col + i]) : 0.f));
-            v[i] = ep.act == 1 ? gelu_erf(t) : t;
-          }
-        }
-        if (EPI == STORE_F32) {
-          float* yp = reinterpret_cast<float*>(ep.y) + orow * ep.ldy + col;
-          if (col + 16 <= ep.n_valid && (ep.ldy & 3) == 0) {
-#pragma unroll
-            for (int i = 0; i < 16; i += 4)
-              *reinterpret_cast<float4*>(yp + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-          } else {
-            for (int i = 0; i < 16; ++i)
-              if (col + i < ep.n_valid) yp[i] = v[i];
-          }
-        } else {
-          __nv_bfloat16* yp = reinterpret_cast<__nv_bfloat16*>(ep.y) + orow * ep.ldy + col;
-          if (col + 16 <= ep.n_valid && (ep.ldy & 7) == 0) {
-            store_bf16x8(yp, v);
-            store_bf16x8(yp + 8, v + 8);
-          } else {
-            for (int i = 0; i < 16; ++i)
-              if (col + i < ep.n_valid) yp[i] = __float2bfloat16_rn(v[i]);
-          }
-        }
-      }
-    } else if (EPI == SWIGLU) {
-      const int F = N / 2;
-      const int o0 = n_tile * (BN / 2);
-      __nv_bfloat16* yp = reinterpret_cast<__nv_bfloat16*>(ep.y) + static_cast<int64_t>(row) * ep.ldy + o0;
-#pragma unroll 1
-      for (int c = 0; c < BN / 2; c += 16) {
-        float g[16], u[16];
-        tmem_ld16(taddr + c, g);
-        tmem_ld16(taddr + BN / 2 + c, u);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float gb = bf16_round(g[i]);
-          g[i] = bf16_round(silu(gb)) * bf16_round(u[i]);
-        }
-        if (row_ok && o0 + c + 16 <= F) {
-          store_bf16x8(yp + c, g);
-          store_bf16x8(yp + c + 8, g + 8);
-        }
-      }
-    } else if (EPI == QKV_ROPE) {
-      const int H = ep.n_heads, HKV = ep.n_kv_heads;
-      const int p = row_ok ? ep.pos[row] : 0;
-      const int rp = row_ok ? (ep.rope_pos ? ep.rope_pos[row] : p) : 0;
-      const int sq = row_ok ? ep.seq[row] : 0;
-      const bool in_cache = p >= 0 && p < ep.cache_len && sq >= 0 && sq < ep.cache_rows;
-      const bool in_rope = rp >= 0 && rp < ep.rope_len;
-      const bool ok = row_ok && in_cache && in_rope;
-      if (row_ok && !(in_cache && in_rope)) raise_error(ERR_BOUNDS);
-      float c[32], s[32];
-      {
-        const float4* cp = reinterpret_cast<const float4*>(ep.cos + static_cast<int64_t>(ok ? rp : 0) * 32);
-        const float4* sp = reinterpret_cast<const float4*>(ep.sin + static_cast<int64_t>(ok ? rp : 0) * 32);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 a = cp[i], b = sp[i];
-          c[4 * i] = a.x; c[4 * i + 1] = a.y; c[4 * i + 2] = a.z; c[4 * i + 3] = a.w;
-          s[4 * i] = b.x; s[4 * i + 1] = b.y; s[4 * i + 2] = b.z; s[4 * i + 3] = b.w;
-        }
-      }
-#pragma unroll 1
-      for (int hh = 0; hh < BN / 64; ++hh) {
-        const int gh = n_tile * (BN / 64) + hh;
+      for (int ch = 0; ch < Chunks<BN>::COUNT; ++ch) {
         float v[64];
-        tmem_ld16(taddr + hh * 64, v);
-        tmem_ld16(taddr + hh * 64 + 16, v + 16);
-        tmem_ld16(taddr + hh * 64 + 32, v + 32);
-        tmem_ld16(taddr + hh * 64 + 48, v + 48);
+#pragma unroll
+        for (int q = 0; q < W; q += 16) tmem_ld16(taddr + chunk_col<BN, EPI>(ch, q), v + q);
         tmem_wait_ld();
-        if (!ok) continue;
+        if (row_ok) epi_chunk<BN, EPI>(ep, row, n_tile, ch, v, r, N);
+      }
+    }
+  } else {
+    // stage this CTA's partial tile (fp32) in shared memory
+    if (epi_warp && have_acc) {
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        tmem_ld16(taddr + c, v);
+        tmem_wait_ld();
+        float4* dst = reinterpret_cast<float4*>(staging + row_local * SROW + c);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) v[i] = bf16_round(v[i]);  // the qkv linear output is stored in bf16
-        if (gh < H) {
-          norm_rope_head(v, ep.q_norm_w, c, s, ep.eps);
-          __nv_bfloat16* qp = ep.q_out + (static_cast<int64_t>(row) * H + gh) * 64;
+        for (int i = 0; i < 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    }
+    cluster_sync();
+    if (epi_warp) {
+      // reduce rows [ks*R, ks*R + R) over the NK partial tiles of the cluster
+      const int t = threadIdx.x - 64;
+      constexpr int G = BN / 4;  // float4 groups per row
+      for (int gidx = t; gidx < R * G; gidx += 128) {
+        const int rr = gidx / G, c4 = gidx % G;
+        const float* src = staging + (ks * R + rr) * SROW + c4 * 4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-          for (int i = 0; i < 64; i += 8) store_bf16x8(qp + i, v + i);
-        } else if (gh < H + 2 * HKV) {
-          const bool is_k = gh < H + HKV;
-          const int kvh = is_k ? gh - H : gh - H - HKV;
-          if (is_k) norm_rope_head(v, ep.k_norm_w, c, s, ep.eps);
-          __nv_bfloat16* cache = is_k ? ep.k_cache : ep.v_cache;
-          __nv_bfloat16* dst =
-              cache + static_cast<int64_t>(sq) * ep.stride_cb + static_cast<int64_t>(p) * ep.stride_cs + kvh * 64;
+        for (int p = 0; p < NK; ++p) {
+          const float4 v = ld_dsmem_f32x4(dsmem_addr(src, static_cast<uint32_t>(p)));
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+        *reinterpret_cast<float4*>(red + rr * SROW + c4 * 4) = acc;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (t < R && have_acc) {
+        const int row = m0 + ks * R + t;
+        if (row < M) {
+          const float r = (EPI != BIAS_ACT && EPI != ADD_RESID) ? row_rscale(ep, row) : 1.f;
+#pragma unroll 1
+          for (int ch = 0; ch < Chunks<BN>::COUNT; ++ch) {
+            float v[64];
 #pragma unroll
-          for (int i = 0; i < 64; i += 8) store_bf16x8(dst + i, v + i);
-          __nv_bfloat16* packed = is_k ? ep.k_out : ep.v_out;
-          if (packed) {
-            __nv_bfloat16* pd = packed + (static_cast<int64_t>(row) * HKV + kvh) * 64;
-#pragma unroll
-            for (int i = 0; i < 64; i += 8) store_bf16x8(pd + i, v + i);
+            for (int i = 0; i < W; ++i) v[i] = red[t * SROW + chunk_col<BN, EPI>(ch, i)];
+            epi_chunk<BN, EPI>(ep, row, n_tile, ch, v, r, N);
           }
         }
       }
     }
+    cluster_sync();
   }
 
   tc_fence_before();

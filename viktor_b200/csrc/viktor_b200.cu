@@ -76,22 +76,47 @@ static int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, 
 static inline unsigned blocks_for(int64_t n, int per) { return static_cast<unsigned>((n + per - 1) / per); }
 
 // ---- GEMM dispatch ----------------------------------------------------------------------------------------
-template <int BN, int STAGES, int EPI>
-static int run_gemm(const void* A, const void* B, int64_t M, int N, int K, const gemm::EpiArgs& ep, int grid_x,
-                    int cluster_x, int64_t b_rows, void* stream) {
-  using L = gemm::Smem<BN, STAGES>;
-  if (M <= 0 || M > (int64_t(1) << 31) - 128) return VK_ERR_ARG;
-  if (K <= 0 || K % gemm::BK != 0) return VK_ERR_ARG;
-  if (!aligned16(A) || !aligned16(B)) return VK_ERR_ARG;
+template <int BN, int EPI, int NK>
+static int run_gemm_nk(const void* A, const void* B, int64_t M, int N, int K, const gemm::EpiArgs& ep, int n_tiles,
+                       int64_t b_rows, void* stream) {
+  using gemm::SmemLayout;
+  const int nkb = K / gemm::BK / NK;
+  const int stages = nkb < gemm::kMaxStages ? nkb : gemm::kMaxStages;
+  const SmemLayout L(BN, NK, stages);
   CUtensorMap ta, tb;
   const uint32_t b_box = EPI == gemm::SWIGLU ? BN / 2 : BN;
   if (!make_map_kmajor(&ta, A, static_cast<uint64_t>(M), K, K, gemm::BM)) return VK_ERR_ARG;
   if (!make_map_kmajor(&tb, B, static_cast<uint64_t>(b_rows), K, K, b_box)) return VK_ERR_ARG;
-  auto kern = gemm::gemm_kernel<BN, STAGES, EPI>;
-  if (!ensure_smem(kern, L::TOTAL)) return VK_ERR_CUDA;
-  dim3 grid(grid_x, static_cast<unsigned>((M + gemm::BM - 1) / gemm::BM));
-  return launch(kern, grid, dim3(gemm::kThreads), L::TOTAL, stream, cluster_x, ta, tb, static_cast<int>(M), N, K,
+  auto kern = gemm::gemm_kernel<BN, EPI, NK>;
+  if (!ensure_smem(kern, SmemLayout(BN, NK, gemm::kMaxStages).total)) return VK_ERR_CUDA;
+  dim3 grid(NK, n_tiles, static_cast<unsigned>((M + gemm::BM - 1) / gemm::BM));
+  return launch(kern, grid, dim3(gemm::kThreads), L.total, stream, NK, ta, tb, static_cast<int>(M), N, K, stages,
                 ep);
+}
+
+// Split-K factor for small-M GEMMs: enough CTAs to cover the SMs (about 128-192), each split at least one
+// 64-wide K block.
+static int pick_nk(int64_t M, int n_tiles, int K) {
+  const int64_t tiles = n_tiles * ((M + gemm::BM - 1) / gemm::BM);
+  const int kb = K / gemm::BK;
+  int nk = 1;
+  while (nk < 8 && tiles * nk * 2 <= 192 && kb % (nk * 2) == 0) nk *= 2;
+  return nk;
+}
+
+template <int BN, int EPI>
+static int run_gemm(const void* A, const void* B, int64_t M, int N, int K, const gemm::EpiArgs& ep, int n_tiles,
+                    int64_t b_rows, int nk, void* stream) {
+  if (M <= 0 || M > (int64_t(1) << 31) - 128) return VK_ERR_ARG;
+  if (K <= 0 || K % gemm::BK != 0 || (K / gemm::BK) % nk != 0) return VK_ERR_ARG;
+  if (!aligned16(A) || !aligned16(B)) return VK_ERR_ARG;
+  switch (nk) {
+    case 1: return run_gemm_nk<BN, EPI, 1>(A, B, M, N, K, ep, n_tiles, b_rows, stream);
+    case 2: return run_gemm_nk<BN, EPI, 2>(A, B, M, N, K, ep, n_tiles, b_rows, stream);
+    case 4: return run_gemm_nk<BN, EPI, 4>(A, B, M, N, K, ep, n_tiles, b_rows, stream);
+    case 8: return run_gemm_nk<BN, EPI, 8>(A, B, M, N, K, ep, n_tiles, b_rows, stream);
+    default: return VK_ERR_ARG;
+  }
 }
 
 static gemm::EpiArgs epi_zero() {
@@ -100,7 +125,7 @@ static gemm::EpiArgs epi_zero() {
   return e;
 }
 
-constexpr int64_t kSmallM = 4096;  // decode-sized GEMMs use narrow tiles (more CTAs), prefill wide tiles
+constexpr int64_t kSmallM = 4096;  // decode-sized GEMMs: narrow tiles + split-K clusters; prefill: wide tiles
 
 }  // namespace vk
 
@@ -168,35 +193,51 @@ int vk_qkv_rope_cache(const void* qkv, const void* q_norm_w, const void* k_norm_
                 n_kv_heads);
 }
 
-int vk_linear(const void* x, const void* w, void* y, int64_t M, int N, int K, int swiglu, int out_f32,
-              void* stream) {
+// Shared body of vk_linear / vk_linear_rmsnorm: plain or SwiGLU GEMM, bf16 or f32 out, optional folded norm.
+static int linear_impl(const void* x, const float* ssq, float eps, const void* w, void* y, int64_t M, int N, int K,
+                       int swiglu, int out_f32, void* stream) {
   if (M == 0) return VK_OK;
   if (!x || !w || !y || N <= 0 || M < 0) return VK_ERR_ARG;
+  if (ssq && (K != 512 || !aligned16(ssq))) return VK_ERR_ARG;
   gemm::EpiArgs ep = epi_zero();
   ep.y = y;
+  ep.ssq_in = ssq;
+  ep.eps = eps;
   if (swiglu) {
     if (out_f32 || N % 2) return VK_ERR_ARG;
     const int F = N / 2;
     ep.ldy = F;
     ep.n_valid = F;
     if (M <= kSmallM) {
-      if (F % 32) return VK_ERR_ARG;
-      return run_gemm<64, 6, gemm::SWIGLU>(x, w, M, N, K, ep, F / 32, 1, N, stream);
+      if (F % 64) return VK_ERR_ARG;
+      return run_gemm<128, gemm::SWIGLU>(x, w, M, N, K, ep, F / 64, N, pick_nk(M, F / 64, K), stream);
     }
     if (F % 128) return VK_ERR_ARG;
-    return run_gemm<256, 4, gemm::SWIGLU>(x, w, M, N, K, ep, F / 128, 1, N, stream);
+    return run_gemm<256, gemm::SWIGLU>(x, w, M, N, K, ep, F / 128, N, 1, stream);
   }
   ep.ldy = N;
   ep.n_valid = N;
   if (out_f32) {
-    if (N <= 16) return run_gemm<16, 6, gemm::STORE_F32>(x, w, M, N, K, ep, 1, 1, N, stream);
-    if (N <= 64) return run_gemm<64, 6, gemm::STORE_F32>(x, w, M, N, K, ep, 1, 1, N, stream);
-    return run_gemm<128, 4, gemm::STORE_F32>(x, w, M, N, K, ep, (N + 127) / 128, 1, N, stream);
+    if (N <= 16) return run_gemm<16, gemm::STORE_F32>(x, w, M, N, K, ep, 1, N, pick_nk(M, 1, K), stream);
+    const int nt = (N + 127) / 128;
+    return run_gemm<128, gemm::STORE_F32>(x, w, M, N, K, ep, nt, N, M <= kSmallM ? pick_nk(M, nt, K) : 1, stream);
   }
-  if (N <= 16) return run_gemm<16, 6, gemm::STORE_BF16>(x, w, M, N, K, ep, 1, 1, N, stream);
-  if (N <= 64 || M <= kSmallM)
-    return run_gemm<64, 6, gemm::STORE_BF16>(x, w, M, N, K, ep, (N + 63) / 64, 1, N, stream);
-  return run_gemm<128, 4, gemm::STORE_BF16>(x, w, M, N, K, ep, (N + 127) / 128, 1, N, stream);
+  if (N <= 64 || M <= kSmallM) {
+    const int nt = (N + 63) / 64;
+    return run_gemm<64, gemm::STORE_BF16>(x, w, M, N, K, ep, nt, N, M <= kSmallM ? pick_nk(M, nt, K) : 1, stream);
+  }
+  return run_gemm<128, gemm::STORE_BF16>(x, w, M, N, K, ep, (N + 127) / 128, N, 1, stream);
+}
+
+int vk_linear(const void* x, const void* w, void* y, int64_t M, int N, int K, int swiglu, int out_f32,
+              void* stream) {
+  return linear_impl(x, nullptr, 0.f, w, y, M, N, K, swiglu, out_f32, stream);
+}
+
+int vk_linear_rmsnorm(const void* x, const float* ssq, float eps, const void* w_folded, void* y, int64_t M, int N,
+                      int K, int swiglu, int out_f32, void* stream) {
+  if (M != 0 && !ssq) return VK_ERR_ARG;
+  return linear_impl(x, ssq, eps, w_folded, y, M, N, K, swiglu, out_f32, stream);
 }
 
 int vk_swiglu(const void* gu, void* out, int64_t n, int F, void* stream) {
@@ -210,12 +251,12 @@ int vk_greedy_update(const float* logits, int64_t ld_logits, const float* bias, 
                      const uint8_t* is_homo, int homo_stop, int64_t* tok, int64_t* run, int64_t* pos,
                      const int64_t* plen, const int64_t* rope_off, int64_t* out, int64_t out_stride,
                      int64_t out_cols, int32_t* pos32, int32_t* seqlens, int32_t* rpos32, int B, int V, int eos,
-                     int pad, const void* emb, const void* norm_w, void* x, void* h, float eps, void* stream) {
+                     int pad, const void* emb, void* x, float* ssq, void* stream) {
   if (B == 0) return VK_OK;
   if (B < 0 || V <= 0 || !logits || !bias || !is_tail || !is_homo || !tok || !run || !pos || !plen || !rope_off ||
       !out || !pos32 || !seqlens || !rpos32)
     return VK_ERR_ARG;
-  if (emb && (!norm_w || !x || !h)) return VK_ERR_ARG;
+  if (emb && (!x || !ssq)) return VK_ERR_ARG;
   ew::GreedyArgs a;
   a.logits = logits;
   a.ld_logits = ld_logits;
@@ -239,10 +280,8 @@ int vk_greedy_update(const float* logits, int64_t ld_logits, const float* bias, 
   a.eos = eos;
   a.pad = pad;
   a.emb = static_cast<const __nv_bfloat16*>(emb);
-  a.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
   a.x = static_cast<__nv_bfloat16*>(emb ? x : nullptr);
-  a.h = static_cast<__nv_bfloat16*>(h);
-  a.eps = eps;
+  a.ssq = ssq;
   return launch(ew::greedy_kernel<512>, dim3(B), dim3(128), 0, stream, 1, a);
 }
 
@@ -323,21 +362,24 @@ int vk_prefill_attention(const void* q, const void* k_cache, const void* v_cache
                 stream, 1, mq, mk, mv, a);
 }
 
-int vk_linear_qkv_rope_cache(const void* h, const void* w_qkv, const void* q_norm_w, const void* k_norm_w,
-                             const float* cos, const float* sin, int rope_len, const int32_t* pos,
-                             const int32_t* rope_pos, const int32_t* seq, void* q, void* k_cache, void* v_cache,
-                             void* k_out, void* v_out, int64_t M, int64_t stride_cb, int64_t stride_cs,
-                             int cache_rows, int cache_len, float eps, int n_heads, int n_kv_heads,
-                             void* stream) {
+int vk_linear_qkv_rope_cache(const void* x, const float* ssq, float norm_eps, const void* w_qkv,
+                             const void* q_norm_w, const void* k_norm_w, const float* cos, const float* sin,
+                             int rope_len, const int32_t* pos, const int32_t* rope_pos, const int32_t* seq, void* q,
+                             void* k_cache, void* v_cache, void* k_out, void* v_out, int64_t M, int64_t stride_cb,
+                             int64_t stride_cs, int cache_rows, int cache_len, float eps, int n_heads,
+                             int n_kv_heads, void* stream) {
   if (M == 0) return VK_OK;
   if (n_heads != 8 || n_kv_heads != 2) return VK_ERR_UNSUPPORTED;
-  if (M < 0 || !h || !w_qkv || !q_norm_w || !k_norm_w || !cos || !sin || !pos || !seq || !q || !k_cache ||
+  if (M < 0 || !x || !w_qkv || !q_norm_w || !k_norm_w || !cos || !sin || !pos || !seq || !q || !k_cache ||
       !v_cache)
     return VK_ERR_ARG;
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || stride_cs % 8 || stride_cb % 8 ||
-      !aligned16(cos) || !aligned16(sin) || (k_out && !aligned16(k_out)) || (v_out && !aligned16(v_out)))
+      !aligned16(cos) || !aligned16(sin) || (k_out && !aligned16(k_out)) || (v_out && !aligned16(v_out)) ||
+      (ssq && !aligned16(ssq)))
     return VK_ERR_ARG;
   gemm::EpiArgs ep = epi_zero();
+  ep.ssq_in = ssq;
+  ep.eps = norm_eps;
   ep.q_out = static_cast<__nv_bfloat16*>(q);
   ep.k_cache = static_cast<__nv_bfloat16*>(k_cache);
   ep.v_cache = static_cast<__nv_bfloat16*>(v_cache);
@@ -357,30 +399,59 @@ int vk_linear_qkv_rope_cache(const void* h, const void* w_qkv, const void* q_nor
   ep.stride_cs = stride_cs;
   ep.n_heads = n_heads;
   ep.n_kv_heads = n_kv_heads;
-  ep.eps = eps;
+  ep.qk_eps = eps;
   const int N = (n_heads + 2 * n_kv_heads) * 64;
-  if (M <= kSmallM) return run_gemm<64, 6, gemm::QKV_ROPE>(h, w_qkv, M, N, 512, ep, N / 64, 1, N, stream);
-  return run_gemm<256, 4, gemm::QKV_ROPE>(h, w_qkv, M, N, 512, ep, N / 256, 1, N, stream);
+  if (M <= kSmallM)
+    return run_gemm<64, gemm::QKV_ROPE>(x, w_qkv, M, N, 512, ep, N / 64, N, pick_nk(M, N / 64, 512), stream);
+  return run_gemm<256, gemm::QKV_ROPE>(x, w_qkv, M, N, 512, ep, N / 256, N, 1, stream);
 }
 
-int vk_linear_add_rmsnorm(const void* a, const void* w, void* x, const void* norm_w, void* h, int64_t M, int K,
-                          float eps, void* stream) {
+int vk_linear_residual(const void* a, const void* w, void* x, float* ssq_out, int64_t M, int K, void* stream) {
   if (M == 0) return VK_OK;
-  if (M < 0 || !a || !w || !x || !norm_w || !h) return VK_ERR_ARG;
-  if (!aligned16(x) || !aligned16(h)) return VK_ERR_ARG;
+  if (M < 0 || !a || !w || !x || !ssq_out) return VK_ERR_ARG;
+  if (!aligned16(x) || !aligned16(ssq_out)) return VK_ERR_ARG;
   gemm::EpiArgs ep = epi_zero();
   ep.x = static_cast<__nv_bfloat16*>(x);
-  ep.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
-  ep.h_out = static_cast<__nv_bfloat16*>(h);
-  ep.eps = eps;
-  if (M <= kSmallM) return run_gemm<64, 6, gemm::ADD_RMSNORM>(a, w, M, 512, K, ep, 8, 8, 512, stream);
-  return run_gemm<256, 4, gemm::ADD_RMSNORM>(a, w, M, 512, K, ep, 2, 2, 512, stream);
+  ep.ssq_out = ssq_out;
+  if (M <= kSmallM) return run_gemm<64, gemm::ADD_RESID>(a, w, M, 512, K, ep, 8, 512, pick_nk(M, 8, K), stream);
+  return run_gemm<256, gemm::ADD_RESID>(a, w, M, 512, K, ep, 2, 512, 1, stream);
+}
+
+int vk_row_ssq(const void* x, float* ssq, int64_t n, int d, void* stream) {
+  if (n == 0) return VK_OK;
+  if (!x || !ssq || n < 0 || d != 512 || !aligned16(x)) return VK_ERR_ARG;
+  return launch(ew::row_ssq_kernel, dim3(blocks_for(n, 8)), dim3(256), 0, stream, 1,
+                static_cast<const __nv_bfloat16*>(x), ssq, n);
+}
+
+int vk_ssq_rmsnorm(const void* x, const float* ssq, const void* w, void* h, int64_t n, int d, float eps,
+                   void* stream) {
+  if (n == 0) return VK_OK;
+  if (!x || !ssq || !w || !h || n < 0 || d != 512 || !aligned16(x) || !aligned16(h)) return VK_ERR_ARG;
+  return launch(ew::ssq_rmsnorm_kernel, dim3(blocks_for(n * 64, 256)), dim3(256), 0, stream, 1,
+                static_cast<const __nv_bfloat16*>(x), ssq, static_cast<const __nv_bfloat16*>(w),
+                static_cast<__nv_bfloat16*>(h), n, eps);
+}
+
+int vk_linear_add_rmsnorm(const void* a, const void* w, void* x, const void* norm_w, void* h, float* ssq_scratch,
+                          int64_t M, int K, float eps, void* stream) {
+  int rc = vk_linear_residual(a, w, x, ssq_scratch, M, K, stream);
+  if (rc != VK_OK) return rc;
+  return vk_ssq_rmsnorm(x, ssq_scratch, norm_w, h, M, 512, eps, stream);
+}
+
+int vk_fold_norm_weight(const void* w, const void* norm_w, void* out, int64_t N, int K, void* stream) {
+  if (N == 0) return VK_OK;
+  if (!w || !norm_w || !out || N < 0 || K <= 0) return VK_ERR_ARG;
+  return launch(ew::fold_norm_kernel, dim3(blocks_for(N * K, 256)), dim3(256), 0, stream, 1,
+                static_cast<const __nv_bfloat16*>(w), static_cast<const __nv_bfloat16*>(norm_w),
+                static_cast<__nv_bfloat16*>(out), N, K);
 }
 
 int vk_linear_bias_act(const void* x, const void* w, const void* bias, void* y, int64_t ldy, const int32_t* row_map,
                        int64_t M, int N, int K, int act, void* stream) {
   if (M == 0) return VK_OK;
-  if (M < 0 || !x || !w || !bias || !y || N <= 0 || N % 16 || ldy < N || (act != 0 && act != 1)) return VK_ERR_ARG;
+  if (M < 0 || !x || !w || !bias || !y || N <= 0 || N % 64 || ldy < N || (act != 0 && act != 1)) return VK_ERR_ARG;
   gemm::EpiArgs ep = epi_zero();
   ep.y = y;
   ep.ldy = ldy;
@@ -388,9 +459,8 @@ int vk_linear_bias_act(const void* x, const void* w, const void* bias, void* y, 
   ep.row_map = row_map;
   ep.bias = static_cast<const __nv_bfloat16*>(bias);
   ep.act = act;
-  if (M <= kSmallM)
-    return run_gemm<64, 6, gemm::BIAS_ACT>(x, w, M, N, K, ep, (N + 63) / 64, 1, N, stream);
-  return run_gemm<128, 4, gemm::BIAS_ACT>(x, w, M, N, K, ep, (N + 127) / 128, 1, N, stream);
+  if (M <= kSmallM) return run_gemm<64, gemm::BIAS_ACT>(x, w, M, N, K, ep, N / 64, N, 1, stream);
+  return run_gemm<128, gemm::BIAS_ACT>(x, w, M, N, K, ep, (N + 127) / 128, N, 1, stream);
 }
 
 int vk_cast_f32_bf16(const float* src, void* dst, int64_t n, void* stream) {

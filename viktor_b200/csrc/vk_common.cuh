@@ -62,12 +62,15 @@ VK_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity to complete.  Returns false if it ran out.
+// Bounded wait for the phase with the given parity to complete.  Returns false if it ran out.  The timer is
+// read once per 64 polls so that the common case costs only the mbarrier probes.
 VK_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
     if (globaltimer() - t0 > kWaitLimitNs) return false;
   }
 }
@@ -110,6 +113,19 @@ VK_DEV uint32_t cluster_ctarank() {
 }
 VK_DEV void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+VK_DEV uint32_t dsmem_addr(const void* local_smem_ptr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local_smem_ptr)), "r"(rank));
+  return remote;
+}
+VK_DEV float4 ld_dsmem_f32x4(uint32_t remote) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
+  return v;
 }
 VK_DEV float ld_dsmem_f32(const void* local_smem_ptr, uint32_t rank) {
   uint32_t remote;

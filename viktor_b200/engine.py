@@ -13,8 +13,8 @@ reused ``out`` buffer, the mutable ``bias`` and the ``cache`` attribute).  Seman
   ``check_every`` steps) or at ``max_new_tokens``.
 
 Every kernel here is this package's CUDA code; there is no CPU or PyTorch fallback.  One decode step is 42
-launches (8 x [qkv+rope+cache GEMM, attention, o GEMM+add+norm, gate_up GEMM+SwiGLU, down GEMM+add+norm],
-lm_head GEMM, greedy+grammar+next embedding), replayed as one CUDA graph.
+launches (8 x [norm+qkv+rope+cache GEMM, attention, o GEMM+residual, norm+gate_up GEMM+SwiGLU, down
+GEMM+residual], norm+lm_head GEMM, greedy+grammar+next embedding), replayed as one CUDA graph.
 """
 
 from __future__ import annotations
@@ -22,6 +22,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
+from . import _lib
 from ._lib import call, check_device_errors, load
 from .config import BOS, EOS, PAD
 from .decoder import KVCache
@@ -117,9 +118,9 @@ class DecodeEngine:
         self.run = torch.zeros(B, dtype=torch.long, device=dev)
         self.plen = torch.zeros(B, dtype=torch.long, device=dev)
 
-        # decode-step activations
+        # decode-step activations: residual x and the block sums of squares of its rows (folded RMSNorms)
         self.x = torch.zeros(B, d, dtype=_BF16, device=dev)
-        self.h = torch.zeros(B, d, dtype=_BF16, device=dev)
+        self.ssq = torch.ones(B, 8, dtype=torch.float32, device=dev)
         self.q = torch.zeros(B, cfg.n_heads, cfg.head_dim, dtype=_BF16, device=dev)
         self.o = torch.zeros(B, cfg.n_heads * cfg.head_dim, dtype=_BF16, device=dev)
         self.g = torch.zeros(B, cfg.ffn_dim, dtype=_BF16, device=dev)
@@ -128,6 +129,7 @@ class DecodeEngine:
         self.attn_ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
         self._pf = None  # prefill buffers, allocated on first prefill
         self.graph = None
+        self.kernels_per_step = 0
         if cuda_graph:
             self._capture()
 
@@ -139,20 +141,20 @@ class DecodeEngine:
         """One greedy step for every sequence (viktor/engine.py:91-97, fused branch)."""
         st = self._stream()
         rp = None if self.pos_scale == 1 else self.rpos32
-        h = self.fast.decode(self.x, self.h, self.pos32, self.rows, self.seqlens, self.cache, self.q, self.o, self.g,
-                             self.attn_ws, rope_pos=rp, stream=st)
-        self._head_select(h, st)
+        self.fast.decode(self.x, self.ssq, self.pos32, self.rows, self.seqlens, self.cache, self.q, self.o, self.g,
+                         self.attn_ws, rope_pos=rp, stream=st)
+        self._head_select(self.x, self.ssq, st)
 
-    def _head_select(self, h, st):
-        """lm_head (fp32 logits) + greedy grammar + state advance + next embedding/first norm."""
+    def _head_select(self, x, ssq, st):
+        """lm_head on the final-normed rows (fp32 logits) + greedy grammar + state advance + the next step's
+        embedding and its sums of squares."""
         w = self.w
-        B = h.shape[0]
-        call("vk_linear", _p(h), _p(w.lm_head), _p(self.logits), B, w.vpad, 512, 0, 1, st)
+        B = x.shape[0]
+        self.fast.logits(x, ssq, self.logits, st)
         call("vk_greedy_update", _p(self.logits), self.logits.stride(0), _p(self.bias), _p(self.is_tail),
              _p(self.is_homo), self.homo_stop, _p(self.tok), _p(self.run), _p(self.pos), _p(self.plen),
              _p(self.rope_off), _p(self.out), self.out.stride(0), self.out.shape[1], _p(self.pos32),
-             _p(self.seqlens), _p(self.rpos32), B, w.vocab, EOS, PAD, _p(w.embed), _p(w.layers[0]["attn_norm"]),
-             _p(self.x), _p(self.h), w.eps, st)
+             _p(self.seqlens), _p(self.rpos32), B, w.vocab, EOS, PAD, _p(w.embed), _p(self.x), _p(self.ssq), st)
 
     @torch.no_grad()
     def _capture(self):
@@ -173,8 +175,10 @@ class DecodeEngine:
                 self._step()
         torch.cuda.current_stream(self.device).wait_stream(s)
         self.graph = torch.cuda.CUDAGraph()
+        before = _lib.launches
         with torch.cuda.graph(self.graph):
             self._step()
+        self.kernels_per_step = _lib.launches - before
         for t, v in zip((self.pos, self.pos32, self.seqlens, self.rpos32, self.tok, self.run), saved):
             t.copy_(v)
         self.out.fill_(PAD)
@@ -209,21 +213,23 @@ class DecodeEngine:
                       fb=torch.empty(frames, self.w.d_enc, dtype=_BF16, device=dev),
                       mid=torch.empty(frames, cfg.d_model, dtype=_BF16, device=dev),
                       x=torch.empty(rows, cfg.d_model, dtype=_BF16, device=dev),
-                      h=torch.empty(rows, cfg.d_model, dtype=_BF16, device=dev),
+                      ssq=torch.empty(rows, 8, dtype=torch.float32, device=dev),
                       q=torch.empty(rows, cfg.n_heads, cfg.head_dim, dtype=_BF16, device=dev),
                       o=torch.empty(rows, cfg.n_heads * cfg.head_dim, dtype=_BF16, device=dev),
                       g=torch.empty(rows, cfg.ffn_dim, dtype=_BF16, device=dev),
                       xl=torch.empty(nb, cfg.d_model, dtype=_BF16, device=dev),
-                      hl=torch.empty(nb, cfg.d_model, dtype=_BF16, device=dev),
+                      sl=torch.empty(nb, 8, dtype=torch.float32, device=dev),
                       ql=torch.empty(nb, cfg.n_heads, cfg.head_dim, dtype=_BF16, device=dev),
                       ol=torch.empty(nb, cfg.n_heads * cfg.head_dim, dtype=_BF16, device=dev),
                       gl=torch.empty(nb, cfg.ffn_dim, dtype=_BF16, device=dev),
-                      hcat=torch.empty(self.B, cfg.d_model, dtype=_BF16, device=dev))
+                      xcat=torch.empty(self.B, cfg.d_model, dtype=_BF16, device=dev),
+                      scat=torch.empty(self.B, 8, dtype=torch.float32, device=dev))
             self._pf = pf
         return pf
 
     def _prefill_sub(self, frames, lens, row0, st):
-        """Projector + packed prefill of chunks row0..row0+len(lens); writes their BOS hidden into hcat."""
+        """Projector + packed prefill of chunks row0..row0+len(lens); writes the final residual of their BOS rows
+        (and its sums of squares) into xcat / scat."""
         w, plan = self.w, self._plan(lens, row0)
         n, nf, total = plan["n"], plan["frames"], plan["total"]
         pf = self._prefill_buffers(total, nf)
@@ -236,18 +242,20 @@ class DecodeEngine:
         # projector: Linear-GELU-Linear; the second GEMM scatters rows into the packed layout
         w0, b0, w1, b1 = w.proj
         mid = pf["mid"][:nf]
-        x, h = pf["x"][:total], pf["h"][:total]
+        x, ssq = pf["x"][:total], pf["ssq"][:total]
         call("vk_linear_bias_act", _p(fb), _p(w0), _p(b0), _p(mid), mid.stride(0), None, nf, 512, w.d_enc, 1, st)
         call("vk_linear_bias_act", _p(mid), _p(w1), _p(b1), _p(x), x.stride(0), _p(plan["frame_idx"]), nf, 512, 512,
              0, st)
         call("vk_scatter_embed", _p(x), _p(plan["last"]), n, total, _p(w.embed), BOS, 512, st)
-        call("vk_add_rmsnorm", _p(x), None, _p(w.layers[0]["attn_norm"]), _p(h), total, 512, w.eps, st)
-        hl = self.fast.prefill(x, h, plan["pos"], plan["seq"], plan["cu"], plan["max_len"], self.cache,
-                               pf["q"][:total], pf["o"][:total], pf["g"][:total], row0=row0, rope_pos=plan["rpos"],
-                               last_indices=plan["last"], lengths=plan["lengths"], x_last=pf["xl"][:n],
-                               h_last=pf["hl"][:n], q_last=pf["ql"][:n], o_last=pf["ol"][:n], g_last=pf["gl"][:n],
-                               workspace=self.attn_ws, stream=st)
-        pf["hcat"][row0:row0 + n].copy_(hl)
+        call("vk_row_ssq", _p(x), _p(ssq), total, 512, st)
+        xl, sl = pf["xl"][:n], pf["sl"][:n]
+        self.fast.prefill(x, ssq, plan["pos"], plan["seq"], plan["cu"], plan["max_len"], self.cache,
+                          pf["q"][:total], pf["o"][:total], pf["g"][:total], row0=row0, rope_pos=plan["rpos"],
+                          last_indices=plan["last"], lengths=plan["lengths"], x_last=xl, ssq_last=sl,
+                          q_last=pf["ql"][:n], o_last=pf["ol"][:n], g_last=pf["gl"][:n], workspace=self.attn_ws,
+                          stream=st)
+        pf["xcat"][row0:row0 + n].copy_(xl)
+        pf["scat"][row0:row0 + n].copy_(sl)
 
     @torch.no_grad()
     def prefill(self, frames, frame_lens):
@@ -268,7 +276,7 @@ class DecodeEngine:
         for lo in range(0, self.B, self.prefill_batch):
             hi = min(self.B, lo + self.prefill_batch)
             self._prefill_sub(frames[int(offs[lo]):int(offs[hi])], frame_lens[lo:hi], lo, st)
-        hcat = self._pf["hcat"][:self.B]
+        xcat, scat = self._pf["xcat"][:self.B], self._pf["scat"][:self.B]
         # first token: select with prev = BOS; greedy writes column pos - plen = 0 and sets pos = plen + 1
         self.tok.fill_(BOS)
         self.run.zero_()
@@ -276,7 +284,7 @@ class DecodeEngine:
         self.plen.copy_(torch.tensor(frame_lens, device=self.device))
         self.pos.copy_(self.plen)
         self.rope_off.copy_(self.plen * (self.pos_scale - 1))
-        self._head_select(hcat, st)
+        self._head_select(xcat, scat, st)
 
     # ------------------------------------------------------------------ decode loop
     @torch.no_grad()
@@ -287,6 +295,7 @@ class DecodeEngine:
         for i in range(n):
             if self.graph is not None:
                 self.graph.replay()
+                _lib.launches += self.kernels_per_step
             else:
                 self._step()
             if steps is None and (i + 1) % self.check_every == 0 and bool(
@@ -330,7 +339,7 @@ class DecodeEngine:
 
         nf = int(P.sum())
         x = torch.empty(total, 512, dtype=_BF16, device=dev)
-        h = torch.empty_like(x)
+        ssq = torch.empty(total, 8, dtype=torch.float32, device=dev)
         fb = torch.empty(nf, w.d_enc, dtype=_BF16, device=dev)
         mid = torch.empty(nf, 512, dtype=_BF16, device=dev)
         frames = frames.to(dev)
@@ -340,16 +349,19 @@ class DecodeEngine:
         call("vk_linear_bias_act", _p(mid), _p(w1), _p(b1), _p(x), 512, _p(t(frame_rows)), nf, 512, 512, 0, st)
         toks = tokens_in.reshape(-1).to(dev, torch.int64).contiguous()
         call("vk_copy_rows", _p(w.embed), _p(toks), w.vocab, _p(x), _p(t(tok_rows)), total, B * T, 1024, st)
-        call("vk_add_rmsnorm", _p(x), None, _p(w.layers[0]["attn_norm"]), _p(h), total, 512, w.eps, st)
+        call("vk_row_ssq", _p(x), _p(ssq), total, 512, st)
         q = torch.empty(total, 8, 64, dtype=_BF16, device=dev)
         o = torch.empty(total, 512, dtype=_BF16, device=dev)
         g = torch.empty(total, self.cfg.ffn_dim, dtype=_BF16, device=dev)
-        hf = self.fast.prefill(x, h, t(pos.astype(np.int32)), t(seq), t(offsets.astype(np.int32)), int(L.max()),
-                               self.cache, q, o, g, row0=0, rope_pos=None if rpos is None else t(rpos), stream=st)
-        ht = torch.empty(B * T, 512, dtype=_BF16, device=dev)
-        call("vk_gather_rows", _p(hf), _p(t(tok_rows)), _p(ht), B * T, 1024, total, st)
+        self.fast.prefill(x, ssq, t(pos.astype(np.int32)), t(seq), t(offsets.astype(np.int32)), int(L.max()),
+                          self.cache, q, o, g, row0=0, rope_pos=None if rpos is None else t(rpos), stream=st)
+        rows = t(tok_rows)
+        xt = torch.empty(B * T, 512, dtype=_BF16, device=dev)
+        st_ = torch.empty(B * T, 8, dtype=torch.float32, device=dev)
+        call("vk_gather_rows", _p(x), _p(rows), _p(xt), B * T, 1024, total, st)
+        call("vk_gather_rows", _p(ssq), _p(rows), _p(st_), B * T, 32, total, st)
         logits = torch.empty(B * T, w.vpad, dtype=torch.float32, device=dev)
-        call("vk_linear", _p(ht), _p(w.lm_head), _p(logits), B * T, w.vpad, 512, 0, 1, st)
+        self.fast.logits(xt, st_, logits, st)
         return logits[:, :w.vocab].reshape(B, T, w.vocab)
 
     def check_errors(self):

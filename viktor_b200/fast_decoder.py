@@ -2,13 +2,15 @@
 
 Tokens are packed [n_tokens, d]: prefill packs the prefixes of many variable-length chunks (cu_seqlens), a
 decode step is one token per sequence.  Per layer (viktor/fast_decoder.py:33-60), with the reference's
-separate ops fused into tensor-core GEMM epilogues:
+separate ops fused into tensor-core GEMM epilogues and every RMSNorm folded into the GEMM that consumes it
+(norm weight in the weight columns, 1/rms per row in the epilogue, from the block sums of squares ssq that the
+producer of the residual x writes):
 
-    q, K/V -> cache  = linear_qkv_rope_cache(h)        (linear + qkv_rope_cache)
+    q, K/V -> cache  = qkv GEMM(x, ssq)                (add_rmsnorm + linear + qkv_rope_cache)
     o                = attention(q, cache)             (prefill: varlen causal; decode / BOS-only: split-K)
-    x += o W_o, h    = linear_add_rmsnorm(o)            (linear + add_rmsnorm)
-    g                = linear(h, gate_up, swiglu)       (linear with SwiGLU epilogue)
-    x += g W_down, h = linear_add_rmsnorm(g)            (linear + add_rmsnorm with the next norm's weight)
+    x += o W_o, ssq  = residual GEMM(o)                (linear + residual add)
+    g                = gate_up GEMM(x, ssq)            (add_rmsnorm + linear + SwiGLU)
+    x += g W_d, ssq  = residual GEMM(g)                (linear + residual add)
 
 The prefill runs the last layer for the BOS rows only (viktor/fast_decoder.py:48-53): all K/V are kept, the
 final signal outputs have no consumer.
@@ -29,7 +31,9 @@ def _p(t):
 
 
 class DeviceWeights:
-    """bf16 device copies of the projector + decoder weights, in the layouts the kernels read."""
+    """bf16 device copies of the projector + decoder weights, in the layouts the kernels read.  The attention
+    norm of each layer is folded into its qkv weight, the MLP norm into gate_up and the final norm into lm_head
+    (columns scaled by the norm weight, rounded once to bf16)."""
 
     def __init__(self, model, device):
         dec = model.decoder
@@ -42,6 +46,12 @@ class DeviceWeights:
         def w(t):
             return t.detach().to(device=device, dtype=_BF16).contiguous()
 
+        def fold(weight, norm):
+            out = torch.empty_like(weight)
+            call("vk_fold_norm_weight", _p(weight), _p(norm), _p(out), weight.shape[0], weight.shape[1],
+                 torch.cuda.current_stream(device).cuda_stream)
+            return out
+
         self.cfg = cfg
         self.eps = float(cfg.norm_eps)
         self.embed = w(dec.embed.weight)
@@ -50,14 +60,14 @@ class DeviceWeights:
         vpad = -(-cfg.vocab_size // 16) * 16
         head = torch.zeros(vpad, cfg.d_model, dtype=_BF16, device=device)
         head[:cfg.vocab_size] = w(dec.lm_head.weight)
-        self.lm_head, self.vpad = head, vpad
         self.norm = w(dec.norm.weight)
+        self.lm_head, self.vpad = fold(head, self.norm), vpad
         self.layers = []
         for blk in dec.layers:
             a = blk.attn
-            self.layers.append(dict(attn_norm=w(blk.attn_norm.weight), qkv=w(a.qkv_proj.weight),
+            self.layers.append(dict(qkv=fold(w(a.qkv_proj.weight), w(blk.attn_norm.weight)),
                                     q_norm=w(a.q_norm.weight), k_norm=w(a.k_norm.weight), o=w(a.o_proj.weight),
-                                    mlp_norm=w(blk.mlp_norm.weight), gate_up=w(blk.gate_up.weight),
+                                    gate_up=fold(w(blk.gate_up.weight), w(blk.mlp_norm.weight)),
                                     down=w(blk.down.weight)))
         cos, sin = rope_tables(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta)
         self.cos, self.sin = cos.to(device).contiguous(), sin.to(device).contiguous()
@@ -66,9 +76,6 @@ class DeviceWeights:
         self.d_enc = proj[0].weight.shape[1]
         if self.d_enc % 64:
             raise NotImplementedError("encoder width must be a multiple of 64")
-
-    def next_norm(self, i):
-        return self.layers[i + 1]["attn_norm"] if i + 1 < len(self.layers) else self.norm
 
 
 class FastDecoder:
@@ -80,60 +87,67 @@ class FastDecoder:
         self.cfg = weights.cfg
 
     # -- helpers -----------------------------------------------------------------------------------------------
-    def _qkv(self, i, h, pos, seq, rope_pos, cache, q_out, stream):
+    def _qkv(self, i, x, ssq, pos, seq, rope_pos, cache, q_out, stream):
         L = self.w.layers[i]
         kc, vc = cache.k[i], cache.v[i]
-        call("vk_linear_qkv_rope_cache", _p(h), _p(L["qkv"]), _p(L["q_norm"]), _p(L["k_norm"]), _p(self.w.cos),
-             _p(self.w.sin), self.w.cos.shape[0], _p(pos), _p(rope_pos), _p(seq), _p(q_out), _p(kc), _p(vc), None,
-             None, h.shape[0], kc.stride(0), kc.stride(1), kc.shape[0], kc.shape[1], self.w.eps, 8, 2, stream)
+        call("vk_linear_qkv_rope_cache", _p(x), _p(ssq), self.w.eps, _p(L["qkv"]), _p(L["q_norm"]), _p(L["k_norm"]),
+             _p(self.w.cos), _p(self.w.sin), self.w.cos.shape[0], _p(pos), _p(rope_pos), _p(seq), _p(q_out), _p(kc),
+             _p(vc), None, None, x.shape[0], kc.stride(0), kc.stride(1), kc.shape[0], kc.shape[1], self.w.eps, 8, 2,
+             stream)
 
     def _decode_attn(self, i, q, lengths, cache, out, workspace, row0, stream):
         kc, vc = cache.k[i], cache.v[i]
         call("vk_decode_attention", _p(q), _p(kc), _p(vc), _p(lengths), _p(out), q.shape[0], row0, kc.shape[0],
              kc.shape[1], kc.stride(0), kc.stride(1), _p(workspace), workspace.numel(), stream)
 
-    def _mlp_tail(self, i, o, x, h, g, stream):
-        """x += o W_o; h = norm(x); g = swiglu(h W_gu); x += g W_d; h = next_norm(x)."""
+    def _mlp_tail(self, i, o, x, ssq, g, stream):
+        """x += o W_o; g = swiglu(norm(x) W_gu); x += g W_d  (ssq tracks the block sums of squares of x)."""
         L = self.w.layers[i]
         M = x.shape[0]
-        call("vk_linear_add_rmsnorm", _p(o), _p(L["o"]), _p(x), _p(L["mlp_norm"]), _p(h), M, 512, self.w.eps, stream)
-        call("vk_linear", _p(h), _p(L["gate_up"]), _p(g), M, L["gate_up"].shape[0], 512, 1, 0, stream)
-        call("vk_linear_add_rmsnorm", _p(g), _p(L["down"]), _p(x), _p(self.w.next_norm(i)), _p(h), M, g.shape[1],
-             self.w.eps, stream)
+        call("vk_linear_residual", _p(o), _p(L["o"]), _p(x), _p(ssq), M, 512, stream)
+        call("vk_linear_rmsnorm", _p(x), _p(ssq), self.w.eps, _p(L["gate_up"]), _p(g), M, L["gate_up"].shape[0], 512,
+             1, 0, stream)
+        call("vk_linear_residual", _p(g), _p(L["down"]), _p(x), _p(ssq), M, g.shape[1], stream)
 
     # -- prefill -----------------------------------------------------------------------------------------------
-    def prefill(self, x, h, pos, seq, cu_seqlens, max_seqlen, cache, q, o, g, row0=0, rope_pos=None,
-                last_indices=None, lengths=None, x_last=None, h_last=None, q_last=None, o_last=None, g_last=None,
+    def prefill(self, x, ssq, pos, seq, cu_seqlens, max_seqlen, cache, q, o, g, row0=0, rope_pos=None,
+                last_indices=None, lengths=None, x_last=None, ssq_last=None, q_last=None, o_last=None, g_last=None,
                 workspace=None, stream=None):
-        """x [n, d] packed prefix embeddings (residual stream, updated in place); h its first attention norm.
-        pos/seq [n] int32; cu_seqlens [b+1] int32.  Fills the cache rows row0.. of those sequences.  Returns the
-        final-normed hidden of every row (h), or with last_indices [b] int64 (+ lengths [b] int32 = T_b and the
-        *_last buffers) only that of each sequence's last row (h_last)."""
+        """x [n, d] packed prefix embeddings (residual stream, updated in place), ssq [n, 8] its block sums of
+        squares; pos/seq [n] int32; cu_seqlens [b+1] int32.  Fills the cache rows row0.. of those sequences.
+        Afterwards x holds the final residual of every row, or with last_indices [b] int64 (+ lengths [b] int32
+        = T_b and the *_last buffers) x_last holds that of each sequence's last row; the matching ssq / ssq_last
+        give the final norm."""
         stream = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
         n_layers = self.cfg.n_layers
         n = x.shape[0]
         for i in range(n_layers):
-            self._qkv(i, h, pos, seq, rope_pos, cache, q, stream)
+            self._qkv(i, x, ssq, pos, seq, rope_pos, cache, q, stream)
             kc, vc = cache.k[i], cache.v[i]
             if last_indices is not None and i == n_layers - 1:
                 b = last_indices.shape[0]
                 call("vk_gather_rows", _p(x), _p(last_indices), _p(x_last), b, 1024, n, stream)
+                call("vk_gather_rows", _p(ssq), _p(last_indices), _p(ssq_last), b, 32, n, stream)
                 call("vk_gather_rows", _p(q), _p(last_indices), _p(q_last), b, 1024, n, stream)
                 self._decode_attn(i, q_last, lengths, cache, o_last, workspace, row0, stream)
-                self._mlp_tail(i, o_last, x_last, h_last, g_last, stream)
-                return h_last
+                self._mlp_tail(i, o_last, x_last, ssq_last, g_last, stream)
+                return
             call("vk_prefill_attention", _p(q), _p(kc), _p(vc), _p(cu_seqlens), cu_seqlens.shape[0] - 1,
                  int(max_seqlen), n, row0, kc.shape[0], kc.shape[1], kc.stride(0), kc.stride(1), _p(o), stream)
-            self._mlp_tail(i, o, x, h, g, stream)
-        return h
+            self._mlp_tail(i, o, x, ssq, g, stream)
 
     # -- one decode step -----------------------------------------------------------------------------------------
-    def decode(self, x, h, pos32, rows, seqlens, cache, q, o, g, workspace, rope_pos=None, stream=None):
-        """One token per sequence: x [B, d] residual, h its first attention norm (from the previous step's
-        greedy kernel); pos32/rows [B] int32; seqlens = pos + 1.  Returns the final-normed hidden h [B, d]."""
+    def decode(self, x, ssq, pos32, rows, seqlens, cache, q, o, g, workspace, rope_pos=None, stream=None):
+        """One token per sequence: x [B, d] residual and ssq [B, 8] (from the previous step's greedy kernel);
+        pos32/rows [B] int32; seqlens = pos + 1.  Leaves the final residual in x (and its ssq)."""
         stream = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
         for i in range(self.cfg.n_layers):
-            self._qkv(i, h, pos32, rows, rope_pos, cache, q, stream)
+            self._qkv(i, x, ssq, pos32, rows, rope_pos, cache, q, stream)
             self._decode_attn(i, q, seqlens, cache, o, workspace, 0, stream)
-            self._mlp_tail(i, o, x, h, g, stream)
-        return h
+            self._mlp_tail(i, o, x, ssq, g, stream)
+
+    def logits(self, x, ssq, out, stream):
+        """fp32 logits of the final-normed rows of x (final norm folded into lm_head)."""
+        w = self.w
+        call("vk_linear_rmsnorm", _p(x), _p(ssq), w.eps, _p(w.lm_head), _p(out), x.shape[0], w.vpad, 512, 0, 1,
+             stream)

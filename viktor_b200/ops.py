@@ -93,16 +93,16 @@ def swiglu(gu):
 
 
 def greedy_update(logits, bias, is_tail, is_homo, homo_stop, tok, run, pos, plen, rope_off, out, pos32, seqlens,
-                  rpos32, eos, pad, emb=None, norm_w=None, x=None, h=None, eps=1e-6):
+                  rpos32, eos, pad, emb=None, x=None, ssq=None):
     """Greedy step bookkeeping in one kernel (viktor/triton_ops.py:200-209).  is_tail / is_homo: bool or uint8
-    [V].  With emb/norm_w/x/h also writes the next step's embedding x and first RMSNorm h."""
+    [V].  With emb/x/ssq also writes the next step's embedding x [B, 512] and its block sums of squares ssq [B, 8]."""
     _check_cuda(logits, tok, out)
     B, V = logits.shape
     it = is_tail.to(torch.uint8) if is_tail.dtype != torch.uint8 else is_tail
     ih = is_homo.to(torch.uint8) if is_homo.dtype != torch.uint8 else is_homo
     call("vk_greedy_update", _p(logits), logits.stride(0), _p(bias), _p(it), _p(ih), int(homo_stop), _p(tok),
          _p(run), _p(pos), _p(plen), _p(rope_off), _p(out), out.stride(0), out.shape[1], _p(pos32), _p(seqlens),
-         _p(rpos32), B, V, eos, pad, _p(emb), _p(norm_w), _p(x), _p(h), eps, _stream(logits))
+         _p(rpos32), B, V, eos, pad, _p(emb), _p(x), _p(ssq), _stream(logits))
 
 
 # ---------------------------------------------------------------- mirror of viktor/decode_attention.py
@@ -152,26 +152,63 @@ def prefill_attention(q, k_cache, v_cache, cu_seqlens, max_seqlen, row0=0, out=N
 
 
 # ---------------------------------------------------------------- fused tensor-core forms (hot path)
-def linear_qkv_rope_cache(h, w_qkv, q_norm_w, k_norm_w, cos, sin, pos, seq, k_cache, v_cache, eps, rope_pos=None,
-                          q_out=None, return_kv=False, n_heads=8, n_kv_heads=2):
-    """h [M, 512] . w_qkv^T with the qkv_rope_cache epilogue: returns q [M, H, 64] (and packed k, v)."""
-    M = h.shape[0]
-    q = q_out if q_out is not None else torch.empty(M, n_heads, 64, dtype=h.dtype, device=h.device)
+def fold_norm_weight(w, norm_w):
+    """W' = bf16(W * norm_w[None, :]): an RMSNorm weight folded into the GEMM that consumes the norm."""
+    out = torch.empty_like(w)
+    call("vk_fold_norm_weight", _p(w.contiguous()), _p(norm_w.contiguous()), _p(out), w.shape[0], w.shape[1],
+         _stream(w))
+    return out
+
+
+def row_ssq(x, out=None):
+    """[n, 8] fp32 sums of squares of the eight 64-column blocks of each row of x [n, 512]."""
+    out = out if out is not None else torch.empty(x.shape[0], 8, dtype=torch.float32, device=x.device)
+    call("vk_row_ssq", _p(x), _p(out), x.shape[0], x.shape[1], _stream(x))
+    return out
+
+
+def linear_rmsnorm(x, ssq, eps, w_folded, swiglu=False, out_dtype=None):
+    """(RMSNorm(x) * w) . W^T given W' = W diag(w) and the row sums of squares of x."""
+    M, K = x.shape
+    N = w_folded.shape[0]
+    out_f32 = out_dtype == torch.float32
+    y = torch.empty(M, N // 2 if swiglu else N, dtype=torch.float32 if out_f32 else x.dtype, device=x.device)
+    call("vk_linear_rmsnorm", _p(x), _p(ssq), eps, _p(w_folded), _p(y), M, N, K, int(bool(swiglu)), int(out_f32),
+         _stream(x))
+    return y
+
+
+def linear_qkv_rope_cache(x, w_qkv, q_norm_w, k_norm_w, cos, sin, pos, seq, k_cache, v_cache, eps, rope_pos=None,
+                          q_out=None, return_kv=False, ssq=None, norm_eps=1e-6, n_heads=8, n_kv_heads=2):
+    """x [M, 512] . w_qkv^T with the qkv_rope_cache epilogue: returns q [M, H, 64] (and packed k, v).  With ssq,
+    x is the residual and w_qkv carries the folded attention-norm weight."""
+    M = x.shape[0]
+    q = q_out if q_out is not None else torch.empty(M, n_heads, 64, dtype=x.dtype, device=x.device)
     k = v = None
     if return_kv:
-        k = torch.empty(M, n_kv_heads, 64, dtype=h.dtype, device=h.device)
+        k = torch.empty(M, n_kv_heads, 64, dtype=x.dtype, device=x.device)
         v = torch.empty_like(k)
-    call("vk_linear_qkv_rope_cache", _p(h), _p(w_qkv), _p(q_norm_w), _p(k_norm_w), _p(cos), _p(sin), cos.shape[0],
-         _p(pos), _p(rope_pos), _p(seq), _p(q), _p(k_cache), _p(v_cache), _p(k), _p(v), M, k_cache.stride(0),
-         k_cache.stride(1), k_cache.shape[0], k_cache.shape[1], eps, n_heads, n_kv_heads, _stream(h))
+    call("vk_linear_qkv_rope_cache", _p(x), _p(ssq), norm_eps, _p(w_qkv), _p(q_norm_w), _p(k_norm_w), _p(cos),
+         _p(sin), cos.shape[0], _p(pos), _p(rope_pos), _p(seq), _p(q), _p(k_cache), _p(v_cache), _p(k), _p(v), M,
+         k_cache.stride(0), k_cache.stride(1), k_cache.shape[0], k_cache.shape[1], eps, n_heads, n_kv_heads,
+         _stream(x))
     return (q, k, v) if return_kv else q
+
+
+def linear_residual(a, w, x, ssq_out=None):
+    """x += a . w^T (bf16, in place); returns the new rows' block sums of squares [M, 8]."""
+    M, K = a.shape
+    ssq = ssq_out if ssq_out is not None else torch.empty(M, 8, dtype=torch.float32, device=a.device)
+    call("vk_linear_residual", _p(a), _p(w), _p(x), _p(ssq), M, K, _stream(a))
+    return ssq
 
 
 def linear_add_rmsnorm(a, w, x, norm_w, eps, h_out=None):
     """x += a . w^T (bf16, in place); returns h = RMSNorm(x) * norm_w.  x, h [M, 512]."""
     M, K = a.shape
     h = h_out if h_out is not None else torch.empty_like(x)
-    call("vk_linear_add_rmsnorm", _p(a), _p(w), _p(x), _p(norm_w), _p(h), M, K, eps, _stream(a))
+    ssq = torch.empty(M, 8, dtype=torch.float32, device=a.device)
+    call("vk_linear_add_rmsnorm", _p(a), _p(w), _p(x), _p(norm_w), _p(h), _p(ssq), M, K, eps, _stream(a))
     return h
 
 
