@@ -33,6 +33,7 @@ constexpr int kCombineOff = kStages * kStageBytes;
 constexpr int kCombineBytes = (4 * 8 * 2 + 4 * 8 * 64) * 4;
 constexpr int kBarOff = kCombineOff + kCombineBytes;
 constexpr int kSmemBytes = kBarOff + 128 + 1024;
+static_assert(kBarOff % 16 == 0 && kCombineOff % 16 == 0, "shared-memory layout alignment");
 
 struct DecodeArgs {
   const __nv_bfloat16* q;   // [nq, 8, 64]
@@ -65,6 +66,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int b = blockIdx.y, split = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+  pdl_launch_dependents();
   pdl_wait();  // q, lengths and the newest cache row come from the previous kernel
   if (b >= a.nq) return;
   const int L = a.lengths[b];
@@ -86,7 +88,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     fence_mbar_init();
   }
   __syncthreads();
-  pdl_launch_dependents();
 
   if (warp == 4) {
     if (lane == 0) {

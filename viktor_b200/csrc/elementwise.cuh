@@ -199,8 +199,18 @@ __global__ void __launch_bounds__(128) greedy_kernel(GreedyArgs a) {
   __shared__ int64_t chosen;
   const int b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_launch_dependents();
   pdl_wait();
   if (b >= a.B) return;
+  // state of this sequence, loaded while the argmax runs
+  int64_t prev = 0, run0 = 0, p = 0, pl = 0, roff = 0;
+  if (tid == 0) {
+    prev = a.tok[b];
+    run0 = a.run[b];
+    p = a.pos[b];
+    pl = a.plen[b];
+    roff = a.rope_off[b];
+  }
   float best = -INFINITY;
   int bi = 0x7fffffff;
   for (int v = tid; v < a.V; v += 128) {
@@ -232,19 +242,17 @@ __global__ void __launch_bounds__(128) greedy_kernel(GreedyArgs a) {
       }
     if (bi == 0x7fffffff) bi = 0;
     int64_t nxt = bi;
-    const int64_t prev = a.tok[b];
     const bool prev_ok = prev >= 0 && prev < a.V;
     if (!prev_ok) raise_error(ERR_BOUNDS);
     if (prev_ok && a.is_tail[prev]) nxt = a.eos;  // a tail must be last
     if (a.homo_stop > 0) {
       const bool same = (nxt == prev) && a.is_homo[nxt];
-      const int64_t run = same ? a.run[b] + 1 : 0;
+      const int64_t run = same ? run0 + 1 : 0;
       a.run[b] = run;
       if (run + 1 >= a.homo_stop) nxt = a.eos;
     }
     if (prev == a.eos || prev == a.pad) nxt = a.pad;
-    int64_t p = a.pos[b];
-    const int64_t col = p - a.plen[b];
+    const int64_t col = p - pl;
     if (col >= 0 && col < a.out_cols)
       a.out[static_cast<int64_t>(b) * a.out_stride + col] = nxt;
     else
@@ -254,7 +262,7 @@ __global__ void __launch_bounds__(128) greedy_kernel(GreedyArgs a) {
     a.pos[b] = p;
     a.pos32[b] = static_cast<int32_t>(p);
     a.seqlens[b] = static_cast<int32_t>(p + 1);
-    a.rpos32[b] = static_cast<int32_t>(p + a.rope_off[b]);
+    a.rpos32[b] = static_cast<int32_t>(p + roff);
     chosen = nxt;
   }
   __syncthreads();
@@ -275,7 +283,6 @@ __global__ void __launch_bounds__(128) greedy_kernel(GreedyArgs a) {
 #pragma unroll
   for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
   if ((tid & 15) == 0) a.ssq[static_cast<int64_t>(b) * 8 + tid / 16] = ss;
-  pdl_launch_dependents();
 }
 
 // Per-row sums of squares of the eight 64-column blocks of x [n, 512] (bf16), one warp per row.

@@ -74,9 +74,12 @@ struct EpiArgs {
 };
 
 // Shared-memory layout (bytes from the 1024-aligned base), identical in every CTA of a launch.
+//   [0, pipe)          TMA ring; after the mainloop, this CTA's fp32 partial tile [128][BN+4] (split-K)
+//   [red_off, ...)     reduced rows [R][BN+4] (split-K)
+//   [bar_off, ...)     mbarriers, TMEM address
 struct SmemLayout {
   int stages, stage_bytes, a_bytes, red_off, bar_off, total;
-  __host__ __device__ SmemLayout(int bn, int nk, int stages_) {
+  __host__ __device__ SmemLayout(int bn, int nk, int stages_, int epi) {
     stages = stages_;
     a_bytes = BM * BK * 2;
     stage_bytes = a_bytes + bn * BK * 2;
@@ -85,7 +88,9 @@ struct SmemLayout {
     if (staging > pipe) pipe = staging;
     pipe = (pipe + 1023) & ~1023;
     red_off = pipe;
-    const int red = nk > 1 ? (BM / nk) * (bn + 4) * 4 : 0;
+    const int R = BM / nk;
+    const int red = nk > 1 ? R * (bn + 4) * 4 : 0;
+    (void)epi;
     bar_off = (red_off + red + 15) & ~15;
     total = bar_off + 128 + 1024;  // barriers + alignment slack
   }
@@ -258,6 +263,127 @@ VK_DEV void epi_chunk(const EpiArgs& ep, int row, int n_tile, int ch, float* v, 
   }
 }
 
+// Split-K epilogue: each thread owns 8 consecutive output columns of one row (SWIGLU: 8 gate + the 8 matching
+// up columns, producing 8 outputs).  Groups of 8 consecutive lanes cover one 64-column block (one head for
+// QKV_ROPE), so row-wide reductions over a block are 3 butterfly shuffles.  Every lane of a warp executes the
+// shuffles; `active` masks the memory traffic of lanes without a row.
+VK_DEV float group8_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  return v;
+}
+
+// Epilogue inputs of one reduced row.
+struct RowInputs {
+  float r;                       // folded-norm row scale
+  int pos, rpos, seq;            // QKV_ROPE
+  const float* cs;               // QKV_ROPE: cos[32] | sin[32] at rpos
+  const __nv_bfloat16* xres;     // ADD_RESID: this CTA's BN columns of the residual row
+};
+
+template <int BN, int EPI>
+VK_DEV void epi_group8(const EpiArgs& ep, int row, int n_tile, int g8, float* v, const RowInputs& in, int N,
+                       bool active) {
+  const float r = in.r;
+  if (EPI == STORE_BF16 || EPI == STORE_F32) {
+    const int col = n_tile * BN + g8 * 8;
+    if (!active) return;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] *= r;
+    if (EPI == STORE_F32) {
+      float* yp = reinterpret_cast<float*>(ep.y) + static_cast<int64_t>(row) * ep.ldy + col;
+      if (col + 8 <= ep.n_valid && (ep.ldy & 3) == 0) {
+        *reinterpret_cast<float4*>(yp) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(yp + 4) = make_float4(v[4], v[5], v[6], v[7]);
+      } else {
+        for (int i = 0; i < 8; ++i)
+          if (col + i < ep.n_valid) yp[i] = v[i];
+      }
+    } else {
+      __nv_bfloat16* yp = reinterpret_cast<__nv_bfloat16*>(ep.y) + static_cast<int64_t>(row) * ep.ldy + col;
+      if (col + 8 <= ep.n_valid && (ep.ldy & 7) == 0) {
+        store_bf16x8(yp, v);
+      } else {
+        for (int i = 0; i < 8; ++i)
+          if (col + i < ep.n_valid) yp[i] = __float2bfloat16_rn(v[i]);
+      }
+    }
+  } else if (EPI == SWIGLU) {
+    const int o0 = n_tile * (BN / 2) + g8 * 8;
+    if (!active || o0 + 8 > N / 2) return;
+    float out[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = bf16_round(silu(bf16_round(v[i] * r))) * bf16_round(v[8 + i] * r);
+    store_bf16x8(reinterpret_cast<__nv_bfloat16*>(ep.y) + static_cast<int64_t>(row) * ep.ldy + o0, out);
+  } else if (EPI == ADD_RESID) {
+    const int c0 = n_tile * BN + g8 * 8;
+    float ss = 0.f;
+    if (active) {
+      __nv_bfloat16* xp = ep.x + static_cast<int64_t>(row) * N + c0;
+      float xo[8];
+      load_bf16x8(in.xres + g8 * 8, xo);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        xo[e] = bf16_round(xo[e] + bf16_round(v[e]));
+        ss += xo[e] * xo[e];
+      }
+      store_bf16x8(xp, xo);
+    }
+    ss = group8_sum(ss);
+    if (active && (g8 & 7) == 0) ep.ssq_out[static_cast<int64_t>(row) * kSsqSlots + c0 / 64] = ss;
+  } else if (EPI == QKV_ROPE) {
+    const int H = ep.n_heads, HKV = ep.n_kv_heads;
+    const int gh = n_tile * (BN / 64) + g8 / 8;
+    const int j = g8 & 7;  // 8-column group within the head
+    const int p = in.pos, sq = in.seq;
+    if (active && (p < 0 || p >= ep.cache_len || sq < 0 || sq >= ep.cache_rows || in.rpos < 0 ||
+                   in.rpos >= ep.rope_len)) {
+      raise_error(ERR_BOUNDS);
+      active = false;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = bf16_round(v[i] * r);  // the qkv linear output is stored in bf16
+    if (gh < H + HKV) {  // uniform across the 8-lane group
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+      ss = group8_sum(ss);
+      const float rr = rsqrtf(ss * (1.0f / 64.0f) + ep.qk_eps);
+      const __nv_bfloat16* wn = gh < H ? ep.q_norm_w : ep.k_norm_w;
+      float y[8], other[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = bf16_round(v[i] * rr * __bfloat162float(wn[j * 8 + i]));
+#pragma unroll
+      for (int i = 0; i < 8; ++i) other[i] = __shfl_xor_sync(0xffffffffu, y[i], 4);
+      const int d0 = (j & 3) * 8;  // position within the rotated half
+      float c[8], sn[8];
+      const float* cp = in.cs + d0;
+      const float* sp = in.cs + 32 + d0;
+      const float4 c0 = *reinterpret_cast<const float4*>(cp), c1 = *reinterpret_cast<const float4*>(cp + 4);
+      const float4 s0 = *reinterpret_cast<const float4*>(sp), s1 = *reinterpret_cast<const float4*>(sp + 4);
+      c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
+      sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)  // first half: y1*c - y2*s; second half: y1*s + y2*c (y1 from the partner)
+        v[i] = j < 4 ? y[i] * c[i] - other[i] * sn[i] : other[i] * sn[i] + y[i] * c[i];
+    }
+    if (!active) return;
+    if (gh < H) {
+      store_bf16x8(ep.q_out + (static_cast<int64_t>(row) * H + gh) * 64 + j * 8, v);
+    } else if (gh < H + 2 * HKV) {
+      const bool is_k = gh < H + HKV;
+      const int kvh = is_k ? gh - H : gh - H - HKV;
+      __nv_bfloat16* cache = is_k ? ep.k_cache : ep.v_cache;
+      store_bf16x8(cache + static_cast<int64_t>(sq) * ep.stride_cb + static_cast<int64_t>(p) * ep.stride_cs +
+                       kvh * 64 + j * 8,
+                   v);
+      __nv_bfloat16* packed = is_k ? ep.k_out : ep.v_out;
+      if (packed) store_bf16x8(packed + (static_cast<int64_t>(row) * HKV + kvh) * 64 + j * 8, v);
+    }
+  }
+}
+
 // TMEM column of element i of chunk ch (SWIGLU chunks gather gate and up halves).
 template <int BN, int EPI>
 VK_DEV int chunk_col(int ch, int i) {
@@ -270,7 +396,7 @@ template <int BN, int EPI, int NK>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                 int K, int stages, EpiArgs ep) {
-  const SmemLayout L(BN, NK, stages);
+  const SmemLayout L(BN, NK, stages, EPI);
   constexpr int B_BOX_BYTES = (EPI == SWIGLU ? BN / 2 : BN) * BK * 2;
   constexpr int SROW = BN + 4;   // staging row stride (floats)
   constexpr int R = BM / NK;     // rows each CTA reduces
@@ -309,6 +435,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Let the next kernel of the stream start its prologue (barriers, TMEM, weight loads) now; it waits for this
+  // grid's completion before touching anything this grid writes.
+  pdl_launch_dependents();
 
   bool ok = true;  // producer / MMA lanes: false once a wait ran out
   if (warp == 0) {
@@ -385,14 +514,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int row_local = quarter * 32 + lane;
   const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
   bool have_acc = false;
-  if (epi_warp) {
-    have_acc = __all_sync(0xffffffffu, mbar_wait(accum, 0));
-    if (!have_acc && lane == 0) raise_error(ERR_WAIT_ACCUM);
-    tc_fence_after();
-  }
-  pdl_launch_dependents();
+  auto wait_accum = [&]() {
+    if (epi_warp) {
+      have_acc = __all_sync(0xffffffffu, mbar_wait(accum, 0));
+      if (!have_acc && lane == 0) raise_error(ERR_WAIT_ACCUM);
+      tc_fence_after();
+    }
+  };
 
   if (NK == 1) {
+    wait_accum();
     if (epi_warp && have_acc) {
       const int row = m0 + row_local;
       const bool row_ok = row < M;
@@ -407,6 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
+    wait_accum();
     // stage this CTA's partial tile (fp32) in shared memory
     if (epi_warp && have_acc) {
 #pragma unroll 1
@@ -439,18 +571,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<float4*>(red + rr * SROW + c4 * 4) = acc;
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (t < R && have_acc) {
-        const int row = m0 + ks * R + t;
-        if (row < M) {
-          const float r = (EPI != BIAS_ACT && EPI != ADD_RESID) ? row_rscale(ep, row) : 1.f;
-#pragma unroll 1
-          for (int ch = 0; ch < Chunks<BN>::COUNT; ++ch) {
-            float v[64];
-#pragma unroll
-            for (int i = 0; i < W; ++i) v[i] = red[t * SROW + chunk_col<BN, EPI>(ch, i)];
-            epi_chunk<BN, EPI>(ep, row, n_tile, ch, v, r, N);
-          }
+      // epilogue over the reduced rows: 8 output columns per thread
+      constexpr int WOUT = EPI == SWIGLU ? BN / 2 : BN;
+      constexpr int TPR = WOUT / 8;          // threads per row
+      constexpr int RPP = 128 / TPR;         // rows per pass
+      const int g8 = t % TPR;
+      for (int base = 0; base < R; base += RPP) {
+        const int rl = base + t / TPR;
+        const int rs = rl < R ? rl : 0;
+        const int row = m0 + ks * R + rl;
+        const bool active = have_acc && rl < R && row < M;
+        RowInputs in;
+        in.r = (active && EPI != ADD_RESID) ? row_rscale(ep, row) : 1.f;
+        in.pos = in.rpos = in.seq = 0;
+        in.cs = nullptr;
+        in.xres = nullptr;
+        if (EPI == QKV_ROPE && active) {
+          in.pos = ep.pos[row];
+          in.rpos = ep.rope_pos ? ep.rope_pos[row] : in.pos;
+          in.seq = ep.seq[row];
         }
+        float cs[64];
+        if (EPI == QKV_ROPE) {
+          const int rp = (active && in.rpos >= 0 && in.rpos < ep.rope_len) ? in.rpos : 0;
+          const int d0 = (g8 & 3) * 8;  // the eight rotation angles this thread needs
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            cs[d0 + i] = ep.cos[static_cast<int64_t>(rp) * 32 + d0 + i];
+            cs[32 + d0 + i] = ep.sin[static_cast<int64_t>(rp) * 32 + d0 + i];
+          }
+          in.cs = cs;
+        }
+        if (EPI == ADD_RESID) in.xres = ep.x + static_cast<int64_t>(active ? row : 0) * N + n_tile * BN;
+        float v[16];
+        const float* src = red + rs * SROW;
+        if (EPI == SWIGLU) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            v[i] = src[g8 * 8 + i];
+            v[8 + i] = src[BN / 2 + g8 * 8 + i];
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = src[g8 * 8 + i];
+        }
+        epi_group8<BN, EPI>(ep, row, n_tile, g8, v, in, N, active);
       }
     }
     cluster_sync();

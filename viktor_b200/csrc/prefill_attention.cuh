@@ -23,6 +23,7 @@ constexpr int kQOff = 0;
 constexpr int kStageOff = kBox;                // stage s: K at kStageOff + s*2*kBox, V right after
 constexpr int kBarOff = kStageOff + kStages * 2 * kBox;
 constexpr int kSmemBytes = kBarOff + 128 + 1024;
+static_assert(kBarOff % 16 == 0 && kStageOff % 1024 == 0, "shared-memory layout alignment");
 
 struct PrefillArgs {
   const int32_t* cu_seqlens;  // [nseq + 1]

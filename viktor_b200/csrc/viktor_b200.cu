@@ -82,13 +82,13 @@ static int run_gemm_nk(const void* A, const void* B, int64_t M, int N, int K, co
   using gemm::SmemLayout;
   const int nkb = K / gemm::BK / NK;
   const int stages = nkb < gemm::kMaxStages ? nkb : gemm::kMaxStages;
-  const SmemLayout L(BN, NK, stages);
+  const SmemLayout L(BN, NK, stages, EPI);
   CUtensorMap ta, tb;
   const uint32_t b_box = EPI == gemm::SWIGLU ? BN / 2 : BN;
   if (!make_map_kmajor(&ta, A, static_cast<uint64_t>(M), K, K, gemm::BM)) return VK_ERR_ARG;
   if (!make_map_kmajor(&tb, B, static_cast<uint64_t>(b_rows), K, K, b_box)) return VK_ERR_ARG;
   auto kern = gemm::gemm_kernel<BN, EPI, NK>;
-  if (!ensure_smem(kern, SmemLayout(BN, NK, gemm::kMaxStages).total)) return VK_ERR_CUDA;
+  if (!ensure_smem(kern, SmemLayout(BN, NK, gemm::kMaxStages, EPI).total)) return VK_ERR_CUDA;
   dim3 grid(NK, n_tiles, static_cast<unsigned>((M + gemm::BM - 1) / gemm::BM));
   return launch(kern, grid, dim3(gemm::kThreads), L.total, stream, NK, ta, tb, static_cast<int>(M), N, K, stages,
                 ep);

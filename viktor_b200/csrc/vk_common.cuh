@@ -119,6 +119,11 @@ VK_DEV uint32_t dsmem_addr(const void* local_smem_ptr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local_smem_ptr)), "r"(rank));
   return remote;
 }
+VK_DEV void st_dsmem_f32x4(uint32_t remote, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(remote), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
 VK_DEV float4 ld_dsmem_f32x4(uint32_t remote) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
