@@ -94,13 +94,19 @@ static int run_gemm_nk(const void* A, const void* B, int64_t M, int N, int K, co
                 ep);
 }
 
-// Split-K factor for small-M GEMMs: enough CTAs to cover the SMs (about 128-192), each split at least one
-// 64-wide K block.
+// Split-K factor for small-M GEMMs.  Measured on B200 at M=256 (chained CUDA-graph launches): with K = 512 and
+// at least 16 output tiles the cluster reduction costs more than it saves, so those run unsplit; deeper or
+// narrower GEMMs (the K = 1536 down projection, the logits) split until about 128-192 CTAs run, each split
+// at least one 64-wide K block, at most VK_MAX_SPLITK (a build-time tuning constant, 8 by default).
+#ifndef VK_MAX_SPLITK
+#define VK_MAX_SPLITK 8
+#endif
 static int pick_nk(int64_t M, int n_tiles, int K) {
   const int64_t tiles = n_tiles * ((M + gemm::BM - 1) / gemm::BM);
   const int kb = K / gemm::BK;
+  if (kb <= 8 && tiles >= 16) return 1;
   int nk = 1;
-  while (nk < 8 && tiles * nk * 2 <= 192 && kb % (nk * 2) == 0) nk *= 2;
+  while (nk < VK_MAX_SPLITK && tiles * nk * 2 <= 192 && kb % (nk * 2) == 0) nk *= 2;
   return nk;
 }
 

@@ -70,7 +70,7 @@ class DecodeEngine:
     def __init__(self, model, batch_size: int, max_new_tokens: int, max_frames: int, backend: str = "auto",
                  cuda_graph: bool = True, prefill_batch: int = 128, check_every: int = 32,
                  attention_backend: str = "auto", temperature: float = 0.0, max_homopolymer: int | None = 64,
-                 device=None):
+                 device=None, decode_groups: int = 2):
         if backend not in ("auto", "cuda", "triton"):
             raise ValueError(f"backend {backend!r}: this engine runs the B200 CUDA kernels only")
         if attention_backend not in ("auto", "cuda", "triton", "flash"):
@@ -127,6 +127,18 @@ class DecodeEngine:
         self.logits = torch.zeros(B, self.w.vpad, dtype=torch.float32, device=dev)
         ws_bytes = load().vk_decode_attention_workspace_bytes(B, max_len)
         self.attn_ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+        # Decode groups: the batch is split into row ranges whose steps run on their own streams, so that one
+        # group's latency-bound projection chain overlaps another group's bandwidth-bound attention.  Every row
+        # is computed exactly as in a single group (the split changes no arithmetic).
+        G = max(1, min(int(decode_groups), B))
+        edges = [B * g // G for g in range(G + 1)]
+        self._groups = []
+        for g in range(G):
+            lo, hi = edges[g], edges[g + 1]
+            ws = torch.zeros(load().vk_decode_attention_workspace_bytes(hi - lo, max_len), dtype=torch.uint8,
+                             device=dev)
+            self._groups.append((lo, hi, ws))
+        self._side_streams = [torch.cuda.Stream(dev) for _ in range(G)] if G > 1 else []
         self._pf = None  # prefill buffers, allocated on first prefill
         self.graph = None
         self.kernels_per_step = 0
@@ -139,22 +151,39 @@ class DecodeEngine:
 
     def _step(self):
         """One greedy step for every sequence (viktor/engine.py:91-97, fused branch)."""
-        st = self._stream()
-        rp = None if self.pos_scale == 1 else self.rpos32
-        self.fast.decode(self.x, self.ssq, self.pos32, self.rows, self.seqlens, self.cache, self.q, self.o, self.g,
-                         self.attn_ws, rope_pos=rp, stream=st)
-        self._head_select(self.x, self.ssq, st)
+        if not self._side_streams:
+            lo, hi, ws = self._groups[0]
+            self._step_rows(lo, hi, ws, self._stream())
+            return
+        main = torch.cuda.current_stream(self.device)
+        for (lo, hi, ws), side in zip(self._groups, self._side_streams):
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                self._step_rows(lo, hi, ws, side.cuda_stream)
+        for side in self._side_streams:
+            main.wait_stream(side)
 
-    def _head_select(self, x, ssq, st):
+    def _step_rows(self, lo, hi, ws, st):
+        """One decode step of the sequences in rows [lo, hi)."""
+        r = slice(lo, hi)
+        rp = None if self.pos_scale == 1 else self.rpos32[r]
+        self.fast.decode(self.x[r], self.ssq[r], self.pos32[r], self.rows[r], self.seqlens[r], self.cache, self.q[r],
+                         self.o[r], self.g[r], ws, rope_pos=rp, stream=st, row0=lo)
+        self._head_select(self.x[r], self.ssq[r], st, lo, hi)
+
+    def _head_select(self, x, ssq, st, lo=0, hi=None):
         """lm_head on the final-normed rows (fp32 logits) + greedy grammar + state advance + the next step's
-        embedding and its sums of squares."""
+        embedding and its sums of squares, for the sequences in rows [lo, hi)."""
         w = self.w
-        B = x.shape[0]
-        self.fast.logits(x, ssq, self.logits, st)
-        call("vk_greedy_update", _p(self.logits), self.logits.stride(0), _p(self.bias), _p(self.is_tail),
-             _p(self.is_homo), self.homo_stop, _p(self.tok), _p(self.run), _p(self.pos), _p(self.plen),
-             _p(self.rope_off), _p(self.out), self.out.stride(0), self.out.shape[1], _p(self.pos32),
-             _p(self.seqlens), _p(self.rpos32), B, w.vocab, EOS, PAD, _p(w.embed), _p(self.x), _p(self.ssq), st)
+        hi = self.B if hi is None else hi
+        r = slice(lo, hi)
+        logits = self.logits[r]
+        self.fast.logits(x, ssq, logits, st)
+        call("vk_greedy_update", _p(logits), logits.stride(0), _p(self.bias), _p(self.is_tail), _p(self.is_homo),
+             self.homo_stop, _p(self.tok[r]), _p(self.run[r]), _p(self.pos[r]), _p(self.plen[r]),
+             _p(self.rope_off[r]), _p(self.out[r]), self.out.stride(0), self.out.shape[1], _p(self.pos32[r]),
+             _p(self.seqlens[r]), _p(self.rpos32[r]), hi - lo, w.vocab, EOS, PAD, _p(w.embed), _p(self.x[r]),
+             _p(self.ssq[r]), st)
 
     @torch.no_grad()
     def _capture(self):
@@ -167,7 +196,7 @@ class DecodeEngine:
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
-            for _ in range(3):
+            for _ in range(3):  # (with decode groups, each group also runs on its own stream here)
                 self.pos.fill_(1)
                 self.pos32.fill_(1)
                 self.seqlens.fill_(2)

@@ -137,13 +137,14 @@ class FastDecoder:
             self._mlp_tail(i, o, x, ssq, g, stream)
 
     # -- one decode step -----------------------------------------------------------------------------------------
-    def decode(self, x, ssq, pos32, rows, seqlens, cache, q, o, g, workspace, rope_pos=None, stream=None):
+    def decode(self, x, ssq, pos32, rows, seqlens, cache, q, o, g, workspace, rope_pos=None, stream=None, row0=0):
         """One token per sequence: x [B, d] residual and ssq [B, 8] (from the previous step's greedy kernel);
-        pos32/rows [B] int32; seqlens = pos + 1.  Leaves the final residual in x (and its ssq)."""
+        pos32/rows [B] int32 (rows = cache row of each sequence, row0 + arange(B)); seqlens = pos + 1.  Leaves
+        the final residual in x (and its ssq)."""
         stream = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
         for i in range(self.cfg.n_layers):
             self._qkv(i, x, ssq, pos32, rows, rope_pos, cache, q, stream)
-            self._decode_attn(i, q, seqlens, cache, o, workspace, 0, stream)
+            self._decode_attn(i, q, seqlens, cache, o, workspace, row0, stream)
             self._mlp_tail(i, o, x, ssq, g, stream)
 
     def logits(self, x, ssq, out, stream):
