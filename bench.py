@@ -204,6 +204,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
     ap.add_argument("--decode-steps", type=int, default=None, help="override the workload's decode steps")
+    ap.add_argument("--batch", type=int, default=None, help="override the workload's chunks per GPU (profiling)")
+    ap.add_argument("--decode-groups", type=int, default=2, help="row groups decoded on concurrent streams")
     ap.add_argument("--cpu-steps", type=int, default=None, help="CPU-baseline decode steps (default: workload's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -211,6 +213,8 @@ def main():
     cfg = dict(CONFIGS[args.config])
     if args.decode_steps:
         cfg["steps"] = args.decode_steps
+    if args.batch:
+        cfg["B"] = args.batch
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -237,7 +241,7 @@ def main():
     dcfg = DecoderConfig(vocab_size=V, rope_theta=1e6)
     model = Basecaller.from_weights(make_weights(dcfg, seed=0, init="normal"), k=cfg["k"], cfg=dcfg)
     lens = make_lens(cfg, B, seed=100 + rank)
-    eng = DecodeEngine(model, B, steps, PLEN, max_homopolymer=None, device=dev)
+    eng = DecodeEngine(model, B, steps, PLEN, max_homopolymer=None, device=dev, decode_groups=args.decode_groups)
     eng.bias[2] = float("-inf")  # EOS masked: fixed-length decode, every step emits a base
     n_bases = torch.as_tensor(model.tokenizer.n_bases, device=dev)
     g = torch.Generator(device=dev)
