@@ -101,6 +101,21 @@ int vk_decode_attention(const void* q, const void* k_cache, const void* v_cache,
                         void* out, int nq, int row0, int cache_rows, int S, int64_t stride_kb, int64_t stride_ks,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* Decode attention for callers that cannot allocate device memory.  No counterpart in the reference: it is
+ * vk_decode_attention with its split-K workspace taken from a fixed array inside this library instead of from
+ * the caller.  Meant for hosts that hand a kernel only its inputs and outputs and have no way to obtain a
+ * workspace: plugin or custom-op interfaces of inference servers that own all device memory, FFI callers
+ * without a CUDA allocator of their own, code that must not allocate once serving has started.
+ * Limits: nq <= 256 queries and S <= 4096 cache positions; larger requests return VK_ERR_ARG with a message on
+ * stderr.  The array (8.25 MiB) lives on every GPU that loads the library until the process exits.  The first
+ * call on a device looks up the array's device address; make that first call before any stream capture.
+ * Every call clears the per-query tickets it uses and then shares the array with all other calls: calls whose
+ * executions overlap on the GPU (concurrent streams, or several devices' work racing on one array per device)
+ * corrupt each other's results — issue them in order on one stream per device. */
+int vk_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, const int32_t* lengths,
+                                void* out, int nq, int row0, int cache_rows, int S, int64_t stride_kb,
+                                int64_t stride_ks, void* stream);
+
 /* flash_attn_varlen_func(q, k, v, cu, cu, max_len, max_len, causal=True) of viktor/fast_decoder.py:73, with K
  * and V read from the cache rows the prefill just wrote.  q, out [n_tok, 8, 64] bf16 packed by cu_seqlens
  * [nseq + 1] (i32, device); sequence b attends cache row row0 + b, positions [0, T_b).  max_seqlen = max T_b. */

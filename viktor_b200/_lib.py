@@ -31,6 +31,7 @@ _SIGS = {
                                p, p]),
     "vk_decode_attention_workspace_bytes": (sz, [i32, i32]),
     "vk_decode_attention": (i32, [p, p, p, p, p, i32, i32, i32, i32, i64, i64, p, sz, p]),
+    "vk_decode_attention_noalloc": (i32, [p, p, p, p, p, i32, i32, i32, i32, i64, i64, p]),
     "vk_prefill_attention": (i32, [p, p, p, p, i32, i32, i64, i32, i32, i32, i64, i64, p, p]),
     "vk_linear_rmsnorm": (i32, [p, p, f32, p, p, i64, i32, i32, i32, i32, p]),
     "vk_linear_qkv_rope_cache": (i32, [p, p, f32, p, p, p, p, p, i32, p, p, p, p, p, p, p, p, i64, i64, i64, i32, i32,

@@ -339,6 +339,54 @@ int vk_decode_attention(const void* q, const void* k_cache, const void* v_cache,
                 mv, a);
 }
 
+}  // extern "C"
+
+// ---- allocation-free decode attention -----------------------------------------------------------------------
+// The split-K workspace of vk_decode_attention_noalloc: sized for 256 queries over 4096 cache positions (16
+// splits of 256).  Zero at module load; each call clears the tickets it uses before the kernel runs.
+namespace vk {
+constexpr int kNoAllocMaxQ = 256;
+constexpr int kNoAllocMaxS = 4096;
+constexpr size_t kNoAllocBytes = 1024 + 256 * 16 * 8 * 2 * 4 + 256 * 16 * 8 * 64 * 4;  // tickets, (m, l), o
+static __device__ __align__(256) uint8_t g_noalloc_attn_scratch[kNoAllocBytes];
+}  // namespace vk
+
+extern "C" {
+
+int vk_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, const int32_t* lengths,
+                                void* out, int nq, int row0, int cache_rows, int S, int64_t stride_kb,
+                                int64_t stride_ks, void* stream) {
+  if (nq == 0) return VK_OK;
+  if (nq < 0 || nq > vk::kNoAllocMaxQ || S <= 0 || S > vk::kNoAllocMaxS) {
+    fprintf(stderr,
+            "viktor_b200: vk_decode_attention_noalloc supports at most %d queries and %d cache positions "
+            "(got %d queries, %d positions); use vk_decode_attention with a caller-provided workspace\n",
+            vk::kNoAllocMaxQ, vk::kNoAllocMaxS, nq, S);
+    return VK_ERR_ARG;
+  }
+  const size_t need = vk_decode_attention_workspace_bytes(nq, S);
+  if (need > vk::kNoAllocBytes) return VK_ERR_ARG;
+  // Device address of the array, looked up once per device with that device current (host code cannot use the
+  // symbol itself as a device pointer).
+  static void* scratch[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VK_ERR_CUDA;
+  if (!scratch[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, vk::g_noalloc_attn_scratch) != cudaSuccess || !p) {
+      fprintf(stderr, "viktor_b200: cannot resolve the decode-attention scratch array on device %d\n", dev);
+      return VK_ERR_CUDA;
+    }
+    scratch[dev] = p;
+  }
+  // the per-query tickets must start at zero (an earlier aborted call could have left them set)
+  const size_t tickets = ((size_t)nq * 4 + 255) / 256 * 256;
+  if (cudaMemsetAsync(scratch[dev], 0, tickets, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return VK_ERR_CUDA;
+  return vk_decode_attention(q, k_cache, v_cache, lengths, out, nq, row0, cache_rows, S, stride_kb, stride_ks,
+                             scratch[dev], vk::kNoAllocBytes, stream);
+}
+
 int vk_prefill_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* cu_seqlens,
                          int nseq, int max_seqlen, int64_t n_tok, int row0, int cache_rows, int S,
                          int64_t stride_kb, int64_t stride_ks, void* out, void* stream) {
