@@ -293,7 +293,7 @@ int vk_greedy_update(const float* logits, int64_t ld_logits, const float* bias, 
 
 size_t vk_decode_attention_workspace_bytes(int nq, int S) {
   if (nq <= 0 || S <= 0) return 0;
-  const size_t splits = (S + attn::kChunk - 1) / attn::kChunk;
+  const size_t splits = (S + attn::kMinChunk - 1) / attn::kMinChunk;
   const size_t counters = ((size_t)nq * 4 + 255) / 256 * 256;
   const size_t ml = ((size_t)nq * splits * 8 * 2 * 4 + 255) / 256 * 256;
   const size_t o = (size_t)nq * splits * 8 * 64 * 4;
@@ -319,7 +319,16 @@ int vk_decode_attention(const void* q, const void* k_cache, const void* v_cache,
   if (workspace_bytes < vk_decode_attention_workspace_bytes(nq, S)) return VK_ERR_ARG;
   CUtensorMap mk, mv;
   if (!make_cache_maps(&mk, &mv, k_cache, v_cache, cache_rows, S, stride_kb, stride_ks)) return VK_ERR_ARG;
-  const int splits = (S + attn::kChunk - 1) / attn::kChunk;
+  const int splits = (S + attn::kMinChunk - 1) / attn::kMinChunk;  // workspace slots per query
+  static int sm_count[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VK_ERR_CUDA;
+  if (!sm_count[dev] && cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return VK_ERR_CUDA;
+  // longest split that still fills every SM with its two resident CTAs (judged on the cache length)
+  int chunk = 1024;
+  while (chunk > attn::kMinChunk && static_cast<int64_t>(nq) * ((S + chunk - 1) / chunk) < 2 * sm_count[dev])
+    chunk /= 2;
   attn::DecodeArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.out = static_cast<__nv_bfloat16*>(out);
@@ -334,9 +343,10 @@ int vk_decode_attention(const void* q, const void* k_cache, const void* v_cache,
   a.ws_ml = reinterpret_cast<float*>(ws + counters);
   a.ws_o = reinterpret_cast<float*>(ws + counters + ((size_t)nq * splits * 8 * 2 * 4 + 255) / 256 * 256);
   a.scale_log2 = 0.125f * 1.4426950408889634f;
+  a.chunk = chunk;
   if (!ensure_smem(attn::decode_attn_kernel, attn::kSmemBytes)) return VK_ERR_CUDA;
-  return launch(attn::decode_attn_kernel, dim3(splits, nq), dim3(attn::kThreads), attn::kSmemBytes, stream, 1, mk,
-                mv, a);
+  return launch(attn::decode_attn_kernel, dim3((S + chunk - 1) / chunk, nq), dim3(attn::kThreads), attn::kSmemBytes,
+                stream, 1, mk, mv, a);
 }
 
 }  // extern "C"
@@ -347,7 +357,8 @@ int vk_decode_attention(const void* q, const void* k_cache, const void* v_cache,
 namespace vk {
 constexpr int kNoAllocMaxQ = 256;
 constexpr int kNoAllocMaxS = 4096;
-constexpr size_t kNoAllocBytes = 1024 + 256 * 16 * 8 * 2 * 4 + 256 * 16 * 8 * 64 * 4;  // tickets, (m, l), o
+constexpr size_t kNoAllocSplits = (kNoAllocMaxS + attn::kMinChunk - 1) / attn::kMinChunk;
+constexpr size_t kNoAllocBytes = 1024 + 256 * kNoAllocSplits * 8 * 2 * 4 + 256 * kNoAllocSplits * 8 * 64 * 4;
 static __device__ __align__(256) uint8_t g_noalloc_attn_scratch[kNoAllocBytes];
 }  // namespace vk
 
