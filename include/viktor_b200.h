@@ -66,8 +66,7 @@ int vk_qkv_rope_cache(const void* qkv, const void* q_norm_w, const void* k_norm_
 
 /* viktor/triton_ops.py:138-146 linear, on tcgen05 tensor cores.  x [M, K] bf16, w [N, K] bf16 (nn.Linear
  * layout).  swiglu = 0: y [M, N] (bf16, or f32 when out_f32).  swiglu = 1: w is gate_up with N = 2F rows (gate
- * rows first) and y [M, F] bf16 = silu(gate) * up.  K a multiple of 64; with swiglu, F a multiple of 32
- * (M <= 4096) or 128 (larger M). */
+ * rows first) and y [M, F] bf16 = silu(gate) * up.  K a multiple of 64; with swiglu, F a multiple of 64. */
 int vk_linear(const void* x, const void* w, void* y, int64_t M, int N, int K, int swiglu, int out_f32,
               void* stream);
 

@@ -9,7 +9,7 @@
 //    chunk (1024, 512 or 256 positions) that still gives a full wave of CTAs: long chunks amortise each CTA's
 //    pipeline fill and split merge (measured: 0.92-0.95 of the copy bandwidth at 1024 vs 0.85 at 256).
 //  * a TMA warp streams 64-position tiles of K and V (one 8 KB box per KV head, 128-byte swizzle) into a
-//    3-stage mbarrier ring; positions past the cache end read as zero.
+//    2-stage mbarrier ring; positions past the cache end read as zero.
 //  * four compute warps each take 16 positions of a tile.  Scores are computed transposed on the warp tensor
 //    cores: S^T[16 pos x 8 heads] = K[16 x (2 x 64)] . Qbd[(2 x 64) x 8], with Qbd block-diagonal (query head
 //    n only sees KV head n / 4), so both KV heads and all 8 query heads go through one MMA chain.  The fp32
@@ -27,7 +27,7 @@ namespace attn {
 
 constexpr int kTile = 64;          // positions per TMA tile
 constexpr int kMinChunk = 256;     // shortest split (positions per CTA); the workspace is sized for it
-constexpr int kStages = 3;
+constexpr int kStages = 2;          // 2 x 32 KB per CTA, 2 CTAs per SM (3 stages measured slower in the full step)
 constexpr int kThreads = 160;      // 4 compute warps + 1 TMA warp
 constexpr int kBoxBytes = 64 * 128;            // 64 positions x 64 bf16 (one KV head)
 constexpr int kStageBytes = 4 * kBoxBytes;     // K h0, K h1, V h0, V h1

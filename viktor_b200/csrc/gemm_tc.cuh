@@ -37,6 +37,9 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
 constexpr int kMaxStages = 4;
+// Stages of the TMA ring: wide tiles get three so that two CTAs fit on an SM (one's epilogue then overlaps the
+// other's mainloop); narrow tiles get four.
+__host__ __device__ constexpr int max_stages_for(int bn) { return bn >= 128 ? 3 : 4; }
 constexpr int kSsqSlots = 8;  // sums of squares per 512-wide residual row, one per 64-column block
 
 enum Epi : int { STORE_BF16 = 0, STORE_F32 = 1, BIAS_ACT = 2, SWIGLU = 3, QKV_ROPE = 4, ADD_RESID = 5 };

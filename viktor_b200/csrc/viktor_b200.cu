@@ -81,14 +81,15 @@ static int run_gemm_nk(const void* A, const void* B, int64_t M, int N, int K, co
                        int64_t b_rows, void* stream) {
   using gemm::SmemLayout;
   const int nkb = K / gemm::BK / NK;
-  const int stages = nkb < gemm::kMaxStages ? nkb : gemm::kMaxStages;
+  constexpr int kStages = gemm::max_stages_for(BN);
+  const int stages = nkb < kStages ? nkb : kStages;
   const SmemLayout L(BN, NK, stages, EPI);
   CUtensorMap ta, tb;
   const uint32_t b_box = EPI == gemm::SWIGLU ? BN / 2 : BN;
   if (!make_map_kmajor(&ta, A, static_cast<uint64_t>(M), K, K, gemm::BM)) return VK_ERR_ARG;
   if (!make_map_kmajor(&tb, B, static_cast<uint64_t>(b_rows), K, K, b_box)) return VK_ERR_ARG;
   auto kern = gemm::gemm_kernel<BN, EPI, NK>;
-  if (!ensure_smem(kern, SmemLayout(BN, NK, gemm::kMaxStages, EPI).total)) return VK_ERR_CUDA;
+  if (!ensure_smem(kern, SmemLayout(BN, NK, kStages, EPI).total)) return VK_ERR_CUDA;
   dim3 grid(NK, n_tiles, static_cast<unsigned>((M + gemm::BM - 1) / gemm::BM));
   return launch(kern, grid, dim3(gemm::kThreads), L.total, stream, NK, ta, tb, static_cast<int>(M), N, K, stages,
                 ep);
@@ -218,8 +219,8 @@ static int linear_impl(const void* x, const float* ssq, float eps, const void* w
       if (F % 64) return VK_ERR_ARG;
       return run_gemm<128, gemm::SWIGLU>(x, w, M, N, K, ep, F / 64, N, pick_nk(M, F / 64, K), stream);
     }
-    if (F % 128) return VK_ERR_ARG;
-    return run_gemm<256, gemm::SWIGLU>(x, w, M, N, K, ep, F / 128, N, 1, stream);
+    if (F % 64) return VK_ERR_ARG;
+    return run_gemm<128, gemm::SWIGLU>(x, w, M, N, K, ep, F / 64, N, 1, stream);
   }
   ep.ldy = N;
   ep.n_valid = N;
@@ -468,7 +469,7 @@ int vk_linear_qkv_rope_cache(const void* x, const float* ssq, float norm_eps, co
   const int N = (n_heads + 2 * n_kv_heads) * 64;
   if (M <= kSmallM)
     return run_gemm<64, gemm::QKV_ROPE>(x, w_qkv, M, N, 512, ep, N / 64, N, pick_nk(M, N / 64, 512), stream);
-  return run_gemm<256, gemm::QKV_ROPE>(x, w_qkv, M, N, 512, ep, N / 256, N, 1, stream);
+  return run_gemm<128, gemm::QKV_ROPE>(x, w_qkv, M, N, 512, ep, N / 128, N, 1, stream);
 }
 
 int vk_linear_residual(const void* a, const void* w, void* x, float* ssq_out, int64_t M, int K, void* stream) {
@@ -479,7 +480,7 @@ int vk_linear_residual(const void* a, const void* w, void* x, float* ssq_out, in
   ep.x = static_cast<__nv_bfloat16*>(x);
   ep.ssq_out = ssq_out;
   if (M <= kSmallM) return run_gemm<64, gemm::ADD_RESID>(a, w, M, 512, K, ep, 8, 512, pick_nk(M, 8, K), stream);
-  return run_gemm<256, gemm::ADD_RESID>(a, w, M, 512, K, ep, 2, 512, 1, stream);
+  return run_gemm<128, gemm::ADD_RESID>(a, w, M, 512, K, ep, 4, 512, 1, stream);
 }
 
 int vk_row_ssq(const void* x, float* ssq, int64_t n, int d, void* stream) {
