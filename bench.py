@@ -284,12 +284,8 @@ def main():
     bases_rank = int(bases.item())
     eng.check_errors()
     if world > 1:
-        t = torch.tensor([elapsed, decode_s, prefill_s], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed, decode_s, prefill_s = t.tolist()
-        b = torch.tensor([bases_rank], device=dev, dtype=torch.long)
-        dist.all_reduce(b)
-        total_bases = int(b.item())
+        from viktor_b200.parallel import reduce_bench
+        elapsed, decode_s, prefill_s, total_bases = reduce_bench(elapsed, decode_s, prefill_s, bases_rank, dev)
     else:
         total_bases = bases_rank
     value = total_bases / elapsed
@@ -313,12 +309,8 @@ def main():
         barrier()
         t_e2e = e0.elapsed_time(e1) / 1e3
         if world > 1:
-            t = torch.tensor([t_e2e], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            t_e2e = t.item()
-            b = torch.tensor([hb], device=dev, dtype=torch.long)
-            dist.all_reduce(b)
-            hb = int(b.item())
+            from viktor_b200.parallel import reduce_bench
+            t_e2e, _, _, hb = reduce_bench(t_e2e, 0.0, 0.0, hb, dev)
         e2e = {"value": hb / t_e2e, "unit": "bases/s", "h2d_bytes_per_step": host_frames.numel() * 4,
                "d2h_bytes_per_step": host_out.numel() * 8}
 
