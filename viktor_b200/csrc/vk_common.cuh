@@ -75,7 +75,7 @@ VK_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
-// ---- TMA (bulk tensor, no multicast) ------------------------------------------------------------------------
+// ---- TMA bulk-tensor loads into this CTA's own shared memory ------------------------------------------------
 VK_DEV void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
