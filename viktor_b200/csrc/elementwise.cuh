@@ -160,7 +160,7 @@ __global__ void swiglu_kernel(const __nv_bfloat16* gu, __nv_bfloat16* out, int64
   const int col = static_cast<int>(i % F);
   const float g = __bfloat162float(gu[row * 2 * F + col]);
   const float u = __bfloat162float(gu[row * 2 * F + F + col]);
-  const float act = bf16_round(g * (1.0f / (1.0f + __expf(-g))));
+  const float act = bf16_round(silu(g));
   out[i] = __float2bfloat16_rn(act * u);
 }
 

@@ -36,10 +36,13 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
-constexpr int kMaxStages = 4;
-// Stages of the TMA ring: wide tiles get three so that two CTAs fit on an SM (one's epilogue then overlaps the
-// other's mainloop); narrow tiles get four.
+constexpr int kMaxStages = 8;
+// Stages of the TMA ring for large M (many tiles per SM): wide tiles get three so that two CTAs fit on an SM
+// (one's epilogue then overlaps the other's mainloop); narrow tiles get four.  Small-M (decode) launches have
+// at most one tile per SM and are bound by load latency: they take as many stages as shared memory holds, up
+// to kMaxStages, so that most or all of a CTA's K blocks are in flight at once.
 __host__ __device__ constexpr int max_stages_for(int bn) { return bn >= 128 ? 3 : 4; }
+constexpr int kSmemBudget = 232448;  // dynamic shared memory one CTA may use on sm_100
 constexpr int kSsqSlots = 8;  // sums of squares per 512-wide residual row, one per 64-column block
 
 enum Epi : int { STORE_BF16 = 0, STORE_F32 = 1, BIAS_ACT = 2, SWIGLU = 3, QKV_ROPE = 4, ADD_RESID = 5 };
@@ -78,10 +81,10 @@ struct EpiArgs {
 
 // Shared-memory layout (bytes from the 1024-aligned base), identical in every CTA of a launch.
 //   [0, pipe)          TMA ring; after the mainloop, this CTA's fp32 partial tile [128][BN+4] (split-K)
-//   [red_off, ...)     reduced rows [R][BN+4] (split-K)
+//   [recv_off, ...)    split-K: slices of the reduced rows received from the peers [NK-1][BM/NK][BN+4]
 //   [bar_off, ...)     mbarriers, TMEM address
 struct SmemLayout {
-  int stages, stage_bytes, a_bytes, red_off, bar_off, total;
+  int stages, stage_bytes, a_bytes, recv_off, bar_off, total;
   __host__ __device__ SmemLayout(int bn, int nk, int stages_, int epi) {
     stages = stages_;
     a_bytes = BM * BK * 2;
@@ -90,12 +93,10 @@ struct SmemLayout {
     const int staging = nk > 1 ? BM * (bn + 4) * 4 : 0;
     if (staging > pipe) pipe = staging;
     pipe = (pipe + 1023) & ~1023;
-    red_off = pipe;
-    const int R = BM / nk;
-    const int red = nk > 1 ? R * (bn + 4) * 4 : 0;
     (void)epi;
-    bar_off = (red_off + red + 15) & ~15;
-    total = bar_off + 128 + 1024;  // barriers + alignment slack
+    recv_off = pipe;  // split-K: the NK-1 slices [BM/nk][bn+4] fp32 sent by the peers
+    bar_off = recv_off + (nk > 1 ? (nk - 1) * (BM / nk) * (bn + 4) * 4 : 0);
+    total = bar_off + 256 + 1024;  // barriers + alignment slack
   }
 };
 
@@ -120,7 +121,6 @@ VK_DEV void load_bf16x8(const __nv_bfloat16* src, float* v) {
 }
 
 VK_DEV float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
-VK_DEV float silu(float g) { return g * (1.0f / (1.0f + __expf(-g))); }
 
 // Row scale of a folded RMSNorm: rsqrt(mean(x^2) + eps) from the producer's eight partial sums.
 VK_DEV float row_rscale(const EpiArgs& ep, int row) {
@@ -277,13 +277,45 @@ VK_DEV float group8_sum(float v) {
   return v;
 }
 
-// Epilogue inputs of one reduced row.
+// Epilogue inputs of one thread's reduced row (split-K), loaded before the accumulator is ready.
 struct RowInputs {
   float r;                       // folded-norm row scale
   int pos, rpos, seq;            // QKV_ROPE
-  const float* cs;               // QKV_ROPE: cos[32] | sin[32] at rpos
-  const __nv_bfloat16* xres;     // ADD_RESID: this CTA's BN columns of the residual row
+  float c[8], s[8];              // QKV_ROPE: cos / sin of the eight rotation angles this thread applies
+  float xres[8];                 // ADD_RESID: this thread's eight residual columns
 };
+
+template <int BN, int EPI>
+VK_DEV RowInputs load_row_inputs(const EpiArgs& ep, int row, int n_tile, int g8, int N, bool valid) {
+  RowInputs in;
+  in.r = (valid && EPI != ADD_RESID) ? row_rscale(ep, row) : 1.f;
+  in.pos = in.rpos = in.seq = 0;
+  if (EPI == QKV_ROPE) {
+    if (valid) {
+      in.pos = ep.pos[row];
+      in.rpos = ep.rope_pos ? ep.rope_pos[row] : in.pos;
+      in.seq = ep.seq[row];
+    }
+    const int rp = (valid && in.rpos >= 0 && in.rpos < ep.rope_len) ? in.rpos : 0;
+    const int d0 = (g8 & 3) * 8;  // position within the rotated half
+    const float4* cp = reinterpret_cast<const float4*>(ep.cos + static_cast<int64_t>(rp) * 32 + d0);
+    const float4* sp = reinterpret_cast<const float4*>(ep.sin + static_cast<int64_t>(rp) * 32 + d0);
+    const float4 c0 = cp[0], c1 = cp[1], s0 = sp[0], s1 = sp[1];
+    in.c[0] = c0.x; in.c[1] = c0.y; in.c[2] = c0.z; in.c[3] = c0.w;
+    in.c[4] = c1.x; in.c[5] = c1.y; in.c[6] = c1.z; in.c[7] = c1.w;
+    in.s[0] = s0.x; in.s[1] = s0.y; in.s[2] = s0.z; in.s[3] = s0.w;
+    in.s[4] = s1.x; in.s[5] = s1.y; in.s[6] = s1.z; in.s[7] = s1.w;
+  }
+  if (EPI == ADD_RESID) {
+    if (valid) {
+      load_bf16x8(ep.x + static_cast<int64_t>(row) * N + n_tile * BN + g8 * 8, in.xres);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) in.xres[i] = 0.f;
+    }
+  }
+  return in;
+}
 
 template <int BN, int EPI>
 VK_DEV void epi_group8(const EpiArgs& ep, int row, int n_tile, int g8, float* v, const RowInputs& in, int N,
@@ -325,10 +357,9 @@ VK_DEV void epi_group8(const EpiArgs& ep, int row, int n_tile, int g8, float* v,
     if (active) {
       __nv_bfloat16* xp = ep.x + static_cast<int64_t>(row) * N + c0;
       float xo[8];
-      load_bf16x8(in.xres + g8 * 8, xo);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        xo[e] = bf16_round(xo[e] + bf16_round(v[e]));
+        xo[e] = bf16_round(in.xres[e] + bf16_round(v[e]));
         ss += xo[e] * xo[e];
       }
       store_bf16x8(xp, xo);
@@ -359,17 +390,9 @@ VK_DEV void epi_group8(const EpiArgs& ep, int row, int n_tile, int g8, float* v,
       for (int i = 0; i < 8; ++i) y[i] = bf16_round(v[i] * rr * __bfloat162float(wn[j * 8 + i]));
 #pragma unroll
       for (int i = 0; i < 8; ++i) other[i] = __shfl_xor_sync(0xffffffffu, y[i], 4);
-      const int d0 = (j & 3) * 8;  // position within the rotated half
-      float c[8], sn[8];
-      const float* cp = in.cs + d0;
-      const float* sp = in.cs + 32 + d0;
-      const float4 c0 = *reinterpret_cast<const float4*>(cp), c1 = *reinterpret_cast<const float4*>(cp + 4);
-      const float4 s0 = *reinterpret_cast<const float4*>(sp), s1 = *reinterpret_cast<const float4*>(sp + 4);
-      c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
-      sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
 #pragma unroll
       for (int i = 0; i < 8; ++i)  // first half: y1*c - y2*s; second half: y1*s + y2*c (y1 from the partner)
-        v[i] = j < 4 ? y[i] * c[i] - other[i] * sn[i] : other[i] * sn[i] + y[i] * c[i];
+        v[i] = j < 4 ? y[i] * in.c[i] - other[i] * in.s[i] : other[i] * in.s[i] + y[i] * in.c[i];
     }
     if (!active) return;
     if (gh < H) {
@@ -410,9 +433,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
   uint64_t* empty = full + kMaxStages;
   uint64_t* accum = empty + kMaxStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* tmem_free = accum + 1;
+  uint64_t* recv_bar = tmem_free + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
   float* staging = reinterpret_cast<float*>(smem);
-  float* red = reinterpret_cast<float*>(smem + L.red_off);
+  float* recv = reinterpret_cast<float*>(smem + L.recv_off);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ks = NK > 1 ? static_cast<int>(blockIdx.x) : 0;
@@ -426,6 +451,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum, 1);
+    mbar_init(tmem_free, 4);
+    mbar_init(recv_bar, 1);
+    if (NK > 1) mbar_expect_tx(recv_bar, static_cast<uint32_t>((NK - 1) * R * SROW * 4));
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -438,6 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (NK > 1) cluster_arrive();  // (phase A) this CTA's receive barrier is initialised
   // Let the next kernel of the stream start its prologue (barriers, TMEM, weight loads) now; it waits for this
   // grid's completion before touching anything this grid writes.
   pdl_launch_dependents();
@@ -456,6 +485,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(sB + B_BOX_BYTES, &tmB, &full[i], kx, N / 2 + n_tile * (BN / 2));
         } else {
           tma_load_2d(sB, &tmB, &full[i], kx, n_tile * BN);
+        }
+      }
+      // The rest of this CTA's weight tiles: into L2 now, so the loads after the wait do not go to HBM.
+      for (int i = pre; i < nkb; ++i) {
+        const int kx = (kb0 + i) * BK;
+        if (EPI == SWIGLU) {
+          tma_prefetch_l2_2d(&tmB, kx, n_tile * (BN / 2));
+          tma_prefetch_l2_2d(&tmB, kx, N / 2 + n_tile * (BN / 2));
+        } else {
+          tma_prefetch_l2_2d(&tmB, kx, n_tile * BN);
         }
       }
       pdl_wait();
@@ -511,7 +550,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---------------- epilogue ----------------
   // tcgen05.ld is warp-collective: every lane of an epilogue warp issues the same loads; only global stores
-  // depend on the row being inside M.
+  // depend on the row being inside M.  Inputs that do not depend on the accumulator (row scales, positions,
+  // RoPE angles, the residual) are loaded before the accumulator wait, while the MMAs run: everything they
+  // read was written before the previous grid completed.
   const bool epi_warp = warp >= 2;
   const int quarter = warp & 3;
   const int row_local = quarter * 32 + lane;
@@ -524,13 +565,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
     }
   };
+  // An epilogue warp is done with TMEM: the MMA warp may free it once all four have said so.
+  auto release_tmem = [&]() {
+    if (epi_warp) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tmem_free);
+    }
+  };
 
   if (NK == 1) {
+    const int row = m0 + row_local;
+    const bool row_ok = row < M;
+    const float r = (epi_warp && row_ok && EPI != BIAS_ACT && EPI != ADD_RESID) ? row_rscale(ep, row) : 1.f;
     wait_accum();
     if (epi_warp && have_acc) {
-      const int row = m0 + row_local;
-      const bool row_ok = row < M;
-      const float r = (row_ok && EPI != BIAS_ACT && EPI != ADD_RESID) ? row_rscale(ep, row) : 1.f;
 #pragma unroll 1
       for (int ch = 0; ch < Chunks<BN>::COUNT; ++ch) {
         float v[64];
@@ -540,93 +589,98 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row_ok) epi_chunk<BN, EPI>(ep, row, n_tile, ch, v, r, N);
       }
     }
+    release_tmem();
   } else {
-    wait_accum();
-    // stage this CTA's partial tile (fp32) in shared memory
-    if (epi_warp && have_acc) {
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        float v[16];
-        tmem_ld16(taddr + c, v);
-        tmem_wait_ld();
-        float4* dst = reinterpret_cast<float4*>(staging + row_local * SROW + c);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-      }
-    }
-    cluster_sync();
+    // Split-K: every CTA of the cluster stages its fp32 partial tile [128][SROW] in its own shared memory and
+    // hands rows [p*R, p*R + R) to CTA p with one bulk copy (the copy engine moves them between the SMs); CTA ks
+    // waits until its NK-1 slices have landed, sums them with its own in the order p = 0..NK-1 and applies the
+    // epilogue.  Each thread owns 8 output columns of one reduced row (SWIGLU: 8 gate + the 8 matching up
+    // columns).  The only cluster-wide wait on this path is before exit: no CTA may leave while a copy still
+    // reads its staging tile.
+    constexpr int WOUT = EPI == SWIGLU ? BN / 2 : BN;
+    constexpr int TPR = WOUT / 8;                 // threads per reduced row
+    constexpr int RPP = 128 / TPR;                // reduced rows per pass
+    constexpr int PASSES = (R + RPP - 1) / RPP;
+    constexpr int NV = EPI == SWIGLU ? 16 : 8;    // values per thread and pass
+    constexpr uint32_t SLICE = R * SROW * 4;      // bytes of one slice
+    static_assert((TPR & (TPR - 1)) == 0 && TPR <= 128, "epilogue thread mapping");
+    static_assert(SLICE % 16 == 0, "bulk copies move multiples of 16 bytes");
+    const int t = epi_warp ? static_cast<int>(threadIdx.x) - 64 : 0;
+    const int g8 = t & (TPR - 1);
+    RowInputs in;
     if (epi_warp) {
-      // reduce rows [ks*R, ks*R + R) over the NK partial tiles of the cluster
-      const int t = threadIdx.x - 64;
-      constexpr int G = BN / 4;  // float4 groups per row
-      for (int gidx = t; gidx < R * G; gidx += 128) {
-        const int rr = gidx / G, c4 = gidx % G;
-        const float* src = staging + (ks * R + rr) * SROW + c4 * 4;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int rl = t / TPR, row = m0 + ks * R + rl;
+      in = load_row_inputs<BN, EPI>(ep, row, n_tile, g8, N, rl < R && row < M);
+    }
+    wait_accum();
+    if (epi_warp) {
+      // stage (on a failed accumulator wait the slices are still sent, so that no peer waits in vain)
+      if (have_acc) {
+        constexpr int CW = BN < 64 ? BN : 64;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += CW) {
+          float v[CW];
+#pragma unroll
+          for (int q = 0; q < CW; q += 16) tmem_ld16(taddr + c0 + q, v + q);
+          tmem_wait_ld();
+          float4* dst = reinterpret_cast<float4*>(staging + row_local * SROW + c0);
+#pragma unroll
+          for (int i = 0; i < CW / 4; ++i)
+            dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+      }
+      release_tmem();
+      fence_proxy_async();                          // staging stores -> visible to the copy engine
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // all 128 rows staged
+      cluster_wait();                               // (phase A) every peer's receive barrier is initialised
+      if (t < NK && t != ks) {
+        const int slot = ks < t ? ks : ks - 1;      // where CTA t keeps the slice from this CTA
+        bulk_copy_to_peer(dsmem_addr(recv + slot * (SLICE / 4), static_cast<uint32_t>(t)),
+                          smem_u32(staging + t * R * SROW), SLICE,
+                          dsmem_addr(recv_bar, static_cast<uint32_t>(t)));
+      }
+      const bool got = mbar_wait(recv_bar, 0);
+      if (!got && t == 0) raise_error(ERR_WAIT_FULL);
+      __syncwarp();
+      cluster_arrive();                             // (phase B) this CTA's slices have all arrived
+#pragma unroll 1
+      for (int pass = 0; pass < PASSES; ++pass) {
+        const int rl = pass * RPP + t / TPR;
+        const int row = m0 + ks * R + rl;
+        const bool active = have_acc && got && rl < R && row < M;
+        if (pass > 0) in = load_row_inputs<BN, EPI>(ep, row, n_tile, g8, N, rl < R && row < M);
+        const int rs = rl < R ? rl : 0;
+        float v[NV];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) v[i] = 0.f;
 #pragma unroll
         for (int p = 0; p < NK; ++p) {
-          const float4 v = ld_dsmem_f32x4(dsmem_addr(src, static_cast<uint32_t>(p)));
-          acc.x += v.x;
-          acc.y += v.y;
-          acc.z += v.z;
-          acc.w += v.w;
-        }
-        *reinterpret_cast<float4*>(red + rr * SROW + c4 * 4) = acc;
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      // epilogue over the reduced rows: 8 output columns per thread
-      constexpr int WOUT = EPI == SWIGLU ? BN / 2 : BN;
-      constexpr int TPR = WOUT / 8;          // threads per row
-      constexpr int RPP = 128 / TPR;         // rows per pass
-      const int g8 = t % TPR;
-      for (int base = 0; base < R; base += RPP) {
-        const int rl = base + t / TPR;
-        const int rs = rl < R ? rl : 0;
-        const int row = m0 + ks * R + rl;
-        const bool active = have_acc && rl < R && row < M;
-        RowInputs in;
-        in.r = (active && EPI != ADD_RESID) ? row_rscale(ep, row) : 1.f;
-        in.pos = in.rpos = in.seq = 0;
-        in.cs = nullptr;
-        in.xres = nullptr;
-        if (EPI == QKV_ROPE && active) {
-          in.pos = ep.pos[row];
-          in.rpos = ep.rope_pos ? ep.rope_pos[row] : in.pos;
-          in.seq = ep.seq[row];
-        }
-        float cs[64];
-        if (EPI == QKV_ROPE) {
-          const int rp = (active && in.rpos >= 0 && in.rpos < ep.rope_len) ? in.rpos : 0;
-          const int d0 = (g8 & 3) * 8;  // the eight rotation angles this thread needs
+          const float* src = p == ks ? staging + (ks * R + rs) * SROW : recv + ((p < ks ? p : p - 1) * R + rs) * SROW;
+          src += g8 * 8;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            cs[d0 + i] = ep.cos[static_cast<int64_t>(rp) * 32 + d0 + i];
-            cs[32 + d0 + i] = ep.sin[static_cast<int64_t>(rp) * 32 + d0 + i];
+          for (int qd = 0; qd < NV / 4; ++qd) {
+            const float4 x = *reinterpret_cast<const float4*>(src + (qd & 1) * 4 + (qd >> 1) * (BN / 2));
+            v[4 * qd] += x.x;
+            v[4 * qd + 1] += x.y;
+            v[4 * qd + 2] += x.z;
+            v[4 * qd + 3] += x.w;
           }
-          in.cs = cs;
-        }
-        if (EPI == ADD_RESID) in.xres = ep.x + static_cast<int64_t>(active ? row : 0) * N + n_tile * BN;
-        float v[16];
-        const float* src = red + rs * SROW;
-        if (EPI == SWIGLU) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            v[i] = src[g8 * 8 + i];
-            v[8 + i] = src[BN / 2 + g8 * 8 + i];
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) v[i] = src[g8 * 8 + i];
         }
         epi_group8<BN, EPI>(ep, row, n_tile, g8, v, in, N, active);
       }
+    } else {
+      __syncwarp();
+      cluster_wait();    // (phase A)
+      cluster_arrive();  // (phase B)
     }
-    cluster_sync();
+    __syncwarp();
+    cluster_wait();  // (phase B) every slice of the cluster has landed: no copy still reads this CTA's staging
   }
 
-  tc_fence_before();
-  __syncthreads();
   if (warp == 1) {
+    // free TMEM only after the four epilogue warps have finished reading it
+    if (!mbar_wait(tmem_free, 0) && lane == 0) raise_error(ERR_WAIT_ACCUM);
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }

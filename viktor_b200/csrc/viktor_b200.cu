@@ -73,7 +73,19 @@ static int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, 
   return VK_OK;
 }
 
+// SMs of the current device (cached per device); 0 if the runtime cannot tell.
+static int device_sm_count() {
+  static int sm_count[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (!sm_count[dev] && cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 0;
+  return sm_count[dev];
+}
+
 static inline unsigned blocks_for(int64_t n, int per) { return static_cast<unsigned>((n + per - 1) / per); }
+
+constexpr int64_t kSmallM = 4096;  // decode-sized GEMMs: narrow tiles + split-K clusters; prefill: wide tiles
 
 // ---- GEMM dispatch ----------------------------------------------------------------------------------------
 template <int BN, int EPI, int NK>
@@ -81,33 +93,38 @@ static int run_gemm_nk(const void* A, const void* B, int64_t M, int N, int K, co
                        int64_t b_rows, void* stream) {
   using gemm::SmemLayout;
   const int nkb = K / gemm::BK / NK;
-  constexpr int kStages = gemm::max_stages_for(BN);
-  const int stages = nkb < kStages ? nkb : kStages;
+  int cap = gemm::max_stages_for(BN);
+  if (M <= kSmallM) {
+    cap = gemm::kMaxStages;
+    while (cap > 2 && SmemLayout(BN, NK, cap, EPI).total > gemm::kSmemBudget) --cap;
+  }
+  const int stages = nkb < cap ? nkb : cap;
   const SmemLayout L(BN, NK, stages, EPI);
   CUtensorMap ta, tb;
   const uint32_t b_box = EPI == gemm::SWIGLU ? BN / 2 : BN;
   if (!make_map_kmajor(&ta, A, static_cast<uint64_t>(M), K, K, gemm::BM)) return VK_ERR_ARG;
   if (!make_map_kmajor(&tb, B, static_cast<uint64_t>(b_rows), K, K, b_box)) return VK_ERR_ARG;
   auto kern = gemm::gemm_kernel<BN, EPI, NK>;
-  if (!ensure_smem(kern, SmemLayout(BN, NK, kStages, EPI).total)) return VK_ERR_CUDA;
+  if (!ensure_smem(kern, gemm::kSmemBudget)) return VK_ERR_CUDA;
   dim3 grid(NK, n_tiles, static_cast<unsigned>((M + gemm::BM - 1) / gemm::BM));
   return launch(kern, grid, dim3(gemm::kThreads), L.total, stream, NK, ta, tb, static_cast<int>(M), N, K, stages,
                 ep);
 }
 
-// Split-K factor for small-M GEMMs.  Measured on B200 at M=256 (chained CUDA-graph launches): with K = 512 and
-// at least 16 output tiles the cluster reduction costs more than it saves, so those run unsplit; deeper or
-// narrower GEMMs (the K = 1536 down projection, the logits) split until about 128-192 CTAs run, each split
-// at least one 64-wide K block, at most VK_MAX_SPLITK (a build-time tuning constant, 8 by default).
+// Split-K factor for small-M GEMMs.  A decode GEMM is bound by latency (load round trips, the epilogue), not
+// by throughput, so it is split over K as far as one wave allows: the largest power of two, at most
+// VK_MAX_SPLITK (a build-time tuning constant, 8 by default), with tiles x splits CTAs on at most one SM each
+// and every split at least one 64-wide K block.  (Measured on B200, chained decode layers in a CUDA graph:
+// a second wave costs more than the shorter K loop saves.)
 #ifndef VK_MAX_SPLITK
 #define VK_MAX_SPLITK 8
 #endif
 static int pick_nk(int64_t M, int n_tiles, int K) {
   const int64_t tiles = n_tiles * ((M + gemm::BM - 1) / gemm::BM);
   const int kb = K / gemm::BK;
-  if (kb <= 8 && tiles >= 16) return 1;
+  const int sms = device_sm_count();
   int nk = 1;
-  while (nk < VK_MAX_SPLITK && tiles * nk * 2 <= 192 && kb % (nk * 2) == 0) nk *= 2;
+  while (nk < VK_MAX_SPLITK && tiles * nk * 2 <= sms && kb % (nk * 2) == 0) nk *= 2;
   return nk;
 }
 
@@ -132,7 +149,6 @@ static gemm::EpiArgs epi_zero() {
   return e;
 }
 
-constexpr int64_t kSmallM = 4096;  // decode-sized GEMMs: narrow tiles + split-K clusters; prefill: wide tiles
 
 }  // namespace vk
 
@@ -217,6 +233,9 @@ static int linear_impl(const void* x, const float* ssq, float eps, const void* w
     ep.n_valid = F;
     if (M <= kSmallM) {
       if (F % 64) return VK_ERR_ARG;
+      // narrow tiles (32 outputs) while they fit in one wave, for more CTAs in flight; else 64 outputs
+      if ((F / 32) * ((M + gemm::BM - 1) / gemm::BM) <= device_sm_count())
+        return run_gemm<64, gemm::SWIGLU>(x, w, M, N, K, ep, F / 32, N, pick_nk(M, F / 32, K), stream);
       return run_gemm<128, gemm::SWIGLU>(x, w, M, N, K, ep, F / 64, N, pick_nk(M, F / 64, K), stream);
     }
     if (F % 64) return VK_ERR_ARG;
@@ -321,15 +340,11 @@ int vk_decode_attention(const void* q, const void* k_cache, const void* v_cache,
   CUtensorMap mk, mv;
   if (!make_cache_maps(&mk, &mv, k_cache, v_cache, cache_rows, S, stride_kb, stride_ks)) return VK_ERR_ARG;
   const int splits = (S + attn::kMinChunk - 1) / attn::kMinChunk;  // workspace slots per query
-  static int sm_count[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VK_ERR_CUDA;
-  if (!sm_count[dev] && cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-    return VK_ERR_CUDA;
+  const int sms = device_sm_count();
+  if (sms <= 0) return VK_ERR_CUDA;
   // longest split that still fills every SM with its two resident CTAs (judged on the cache length)
   int chunk = 1024;
-  while (chunk > attn::kMinChunk && static_cast<int64_t>(nq) * ((S + chunk - 1) / chunk) < 2 * sm_count[dev])
-    chunk /= 2;
+  while (chunk > attn::kMinChunk && static_cast<int64_t>(nq) * ((S + chunk - 1) / chunk) < 2 * sms) chunk /= 2;
   attn::DecodeArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.out = static_cast<__nv_bfloat16*>(out);

@@ -35,6 +35,11 @@ VK_DEV uint64_t globaltimer() {
   return t;
 }
 
+// silu(g) = g * sigmoid(g) with the fast exponential and the fast (branch-free) reciprocal: a few ulp in fp32,
+// far below the bf16 rounding that follows every use; the IEEE reciprocal's slow-path branch serialises an
+// unrolled epilogue.
+VK_DEV float silu(float g) { return g * __fdividef(1.0f, 1.0f + __expf(-g)); }
+
 VK_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
 // ---- mbarrier ---------------------------------------------------------------------------------------------
@@ -101,6 +106,13 @@ VK_DEV void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
       : "memory");
 }
 
+// Bulk-tensor prefetch of a tile into L2 (no shared-memory destination, no completion to wait for).
+VK_DEV void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 // ---- programmatic dependent launch ---------------------------------------------------------------------------
 VK_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 VK_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -114,6 +126,9 @@ VK_DEV uint32_t cluster_ctarank() {
 VK_DEV void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// The two halves of cluster_sync, for work that can sit between arriving and waiting.
+VK_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+VK_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 VK_DEV uint32_t dsmem_addr(const void* local_smem_ptr, uint32_t rank) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local_smem_ptr)), "r"(rank));
@@ -138,6 +153,16 @@ VK_DEV float ld_dsmem_f32(const void* local_smem_ptr, uint32_t rank) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
   return v;
+}
+
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from this CTA's shared memory into
+// a peer CTA's shared memory; completion is signalled on the peer's mbarrier (complete_tx).  Addresses of the
+// peer come from dsmem_addr.
+VK_DEV void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes, uint32_t bar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst_cluster),
+               "r"(src_cta), "r"(bytes), "r"(bar_cluster)
+               : "memory");
 }
 
 // ---- tcgen05 -------------------------------------------------------------------------------------------------
