@@ -96,6 +96,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
+      const uint64_t stream_policy = l2_policy_evict_first();  // the cache is read once per step
       for (int t = 0; t < ntiles; ++t) {
         const int s = t % kStages;
         const uint32_t ph = (t / kStages) & 1;
@@ -106,10 +107,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint8_t* st = smem + s * kStageBytes;
         const int p0 = p_begin + t * kTile;
         mbar_expect_tx(&full[s], kStageBytes);
-        tma_load_4d(st, &tmK, &full[s], 0, 0, p0, crow);
-        tma_load_4d(st + kBoxBytes, &tmK, &full[s], 0, 1, p0, crow);
-        tma_load_4d(st + 2 * kBoxBytes, &tmV, &full[s], 0, 0, p0, crow);
-        tma_load_4d(st + 3 * kBoxBytes, &tmV, &full[s], 0, 1, p0, crow);
+        tma_load_4d_hint(st, &tmK, &full[s], 0, 0, p0, crow, stream_policy);
+        tma_load_4d_hint(st + kBoxBytes, &tmK, &full[s], 0, 1, p0, crow, stream_policy);
+        tma_load_4d_hint(st + 2 * kBoxBytes, &tmV, &full[s], 0, 0, p0, crow, stream_policy);
+        tma_load_4d_hint(st + 3 * kBoxBytes, &tmV, &full[s], 0, 1, p0, crow, stream_policy);
       }
     }
     return;

@@ -474,17 +474,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool ok = true;  // producer / MMA lanes: false once a wait ran out
   if (warp == 0) {
     if (lane == 0) {
-      // The B operand (weights) does not depend on the previous kernel: start it before waiting on it.
+      // The B operand (weights) does not depend on the previous kernel: start it before waiting on it.  Weights
+      // are re-read every step: keep them in L2 ahead of streamed data.
+      const uint64_t keep = l2_policy_evict_last();
       const int pre = nkb < stages ? nkb : stages;
       for (int i = 0; i < pre; ++i) {
         uint8_t* sB = smem + i * L.stage_bytes + L.a_bytes;
         const int kx = (kb0 + i) * BK;
         mbar_expect_tx(&full[i], L.stage_bytes);
         if (EPI == SWIGLU) {
-          tma_load_2d(sB, &tmB, &full[i], kx, n_tile * (BN / 2));
-          tma_load_2d(sB + B_BOX_BYTES, &tmB, &full[i], kx, N / 2 + n_tile * (BN / 2));
+          tma_load_2d_hint(sB, &tmB, &full[i], kx, n_tile * (BN / 2), keep);
+          tma_load_2d_hint(sB + B_BOX_BYTES, &tmB, &full[i], kx, N / 2 + n_tile * (BN / 2), keep);
         } else {
-          tma_load_2d(sB, &tmB, &full[i], kx, n_tile * BN);
+          tma_load_2d_hint(sB, &tmB, &full[i], kx, n_tile * BN, keep);
         }
       }
       // The rest of this CTA's weight tiles: into L2 now, so the loads after the wait do not go to HBM.
@@ -513,10 +515,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_expect_tx(&full[s], L.stage_bytes);
         tma_load_2d(sA, &tmA, &full[s], kx, m0);
         if (EPI == SWIGLU) {
-          tma_load_2d(sB, &tmB, &full[s], kx, n_tile * (BN / 2));
-          tma_load_2d(sB + B_BOX_BYTES, &tmB, &full[s], kx, N / 2 + n_tile * (BN / 2));
+          tma_load_2d_hint(sB, &tmB, &full[s], kx, n_tile * (BN / 2), keep);
+          tma_load_2d_hint(sB + B_BOX_BYTES, &tmB, &full[s], kx, N / 2 + n_tile * (BN / 2), keep);
         } else {
-          tma_load_2d(sB, &tmB, &full[s], kx, n_tile * BN);
+          tma_load_2d_hint(sB, &tmB, &full[s], kx, n_tile * BN, keep);
         }
       }
     } else {

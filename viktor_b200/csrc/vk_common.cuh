@@ -106,6 +106,35 @@ VK_DEV void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
       : "memory");
 }
 
+// L2 eviction priorities for TMA loads (createpolicy): a stream read once (the KV cache in decode attention)
+// is marked evict-first so that it does not push the small, re-read working set (weights, activations) out of
+// L2; the weights are marked evict-last.
+VK_DEV uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+VK_DEV uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+VK_DEV void tma_load_2d_hint(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, "
+      "%4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+VK_DEV void tma_load_4d_hint(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z, int w,
+                             uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, "
+      "%4, %5, %6}], [%2], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w), "l"(policy)
+      : "memory");
+}
+
 // Bulk-tensor prefetch of a tile into L2 (no shared-memory destination, no completion to wait for).
 VK_DEV void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
