@@ -114,8 +114,9 @@ static int run_gemm_nk(const void* A, const void* B, int64_t M, int N, int K, co
 // Split-K factor for small-M GEMMs.  A decode GEMM is bound by latency (load round trips, the epilogue), not
 // by throughput, so it is split over K as far as one wave allows: the largest power of two, at most
 // VK_MAX_SPLITK (a build-time tuning constant, 8 by default), with tiles x splits CTAs on at most one SM each
-// and every split at least one 64-wide K block.  (Measured on B200, chained decode layers in a CUDA graph:
-// a second wave costs more than the shorter K loop saves.)
+// and every split at least two 64-wide K blocks.  (Measured on B200, full decode steps with two row groups in
+// one CUDA graph: a second wave costs more than the shorter K loop saves, and one-block splits cost more in
+// the reduction than they save in the K loop.)
 #ifndef VK_MAX_SPLITK
 #define VK_MAX_SPLITK 8
 #endif
@@ -124,7 +125,7 @@ static int pick_nk(int64_t M, int n_tiles, int K) {
   const int kb = K / gemm::BK;
   const int sms = device_sm_count();
   int nk = 1;
-  while (nk < VK_MAX_SPLITK && tiles * nk * 2 <= sms && kb % (nk * 2) == 0) nk *= 2;
+  while (nk < VK_MAX_SPLITK && tiles * nk * 2 <= sms && kb % (nk * 2) == 0 && kb / (nk * 2) >= 2) nk *= 2;
   return nk;
 }
 
