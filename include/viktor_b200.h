@@ -85,6 +85,18 @@ int vk_greedy_update(const float* logits, int64_t ld_logits, const float* bias, 
                      int64_t out_cols, int32_t* pos32, int32_t* seqlens, int32_t* rpos32, int B, int V, int eos,
                      int pad, const void* emb, void* x, float* ssq, void* stream);
 
+/* viktor/engine.py:79-89 _select at temperature > 0 (Gumbel-max sampling) + the state advance of
+ * vk_greedy_update.  Arguments as vk_greedy_update, plus noise [B, V] f32 uniform draws in [0, 1) (row stride
+ * ld_noise >= V; the torch.rand_like of viktor/engine.py:82, drawn by the caller) and temperature > 0:
+ * score = (logits + bias) / temperature - log(-log(max(noise, 1e-20))), argmax (ties to the lower index),
+ * then the grammar. */
+int vk_sample_update(const float* logits, int64_t ld_logits, const float* bias, const uint8_t* is_tail,
+                     const uint8_t* is_homo, int homo_stop, int64_t* tok, int64_t* run, int64_t* pos,
+                     const int64_t* plen, const int64_t* rope_off, int64_t* out, int64_t out_stride,
+                     int64_t out_cols, int32_t* pos32, int32_t* seqlens, int32_t* rpos32, int B, int V, int eos,
+                     int pad, const void* emb, void* x, float* ssq, const float* noise, int64_t ld_noise,
+                     float temperature, void* stream);
+
 /* ---- attention: viktor/decode_attention.py, flash_attn calls of viktor/fast_decoder.py ------------------- */
 
 /* Workspace bytes vk_decode_attention needs for nq queries over a cache of S positions. */

@@ -7,7 +7,9 @@ files.  Inputs are not stored: weights and frames are regenerated from seeds by
 
 Each fixture holds, for one model configuration:
   * ``tokens``      reference greedy tokens, ``DecodeEngine(backend="torch").generate``
-                    (viktor/engine.py:168-220)
+                    (viktor/engine.py:168-220); sampled tokens for the cases with a temperature
+  * ``noise``       (sampled cases) the uniform draws [max_new, B, V] that stood in for ``torch.rand_like`` in
+                    the reference's selection (viktor/engine.py:82), one per selected token, seeded
   * ``tf_logits``   teacher-forced logits per chunk, ``Basecaller.logits`` (viktor/model.py:55-60)
   * ``tf_tokens``   the teacher-forcing inputs used for them ([BOS] + seeded tokens)
   * ``meta``        JSON: config, seeds, lengths, engine settings
@@ -52,6 +54,12 @@ CASES = {
     # larger batch for token agreement on the GPU
     "base_b8": dict(k=1, cfg=dict(rope_theta=1e6), lens=[1, 64, 127, 128, 129, 200, 255, 300], max_new=40,
                     mask_eos=True, max_homopolymer=None, weight_seed=11, frame_seed=12, tf_len=16),
+    # sampled decoding (viktor/engine.py:81-82): Gumbel-perturbed argmax at temperature 0.7 / 1.0
+    "sampled_t07": dict(k=1, cfg=dict(rope_theta=1e6), lens=[9, 40, 23], max_new=16, mask_eos=False,
+                        max_homopolymer=64, weight_seed=15, frame_seed=16, tf_len=6, temperature=0.7, noise_seed=17),
+    "sampled_kmer4": dict(k=4, cfg=dict(rope_theta=1e6), lens=[14, 31], max_new=14, mask_eos=False,
+                          max_homopolymer=64, weight_seed=18, frame_seed=19, tf_len=6, temperature=1.0,
+                          noise_seed=20),
     # the reference's own unit-test model shape (tests/test_viktor.py:25-30): oracle generality only
     "tiny": dict(k=4, cfg=dict(d_model=32, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=8, ffn_dim=64,
                               max_seq_len=512), d_enc=32, lens=[64, 128, 64], max_new=20, mask_eos=False,
@@ -74,14 +82,31 @@ def run_case(name, c, viktor):
     lens = c["lens"]
     frames = make_frames(lens, d_enc=d_enc, seed=c["frame_seed"])
     B = len(lens)
+    T = c.get("temperature", 0.0)
+    noise = None
+    rand_like = torch.rand_like
+    if T > 0:
+        noise = np.random.default_rng(c["noise_seed"]).random((c["max_new"], B, tok.vocab_size), dtype=np.float32)
+        drawn = [0]
+
+        def seeded_rand_like(t, **kw):  # the reference's only random draw: one [B, V] per selection
+            assert tuple(t.shape) == (B, tok.vocab_size)
+            u = torch.from_numpy(noise[drawn[0]].copy())
+            drawn[0] += 1
+            return u
+
+        torch.rand_like = seeded_rand_like
     with torch.no_grad():
         eng = DecodeEngine(model, B, c["max_new"], max(lens), backend="torch", cuda_graph=False,
-                           max_homopolymer=c["max_homopolymer"])
+                           max_homopolymer=c["max_homopolymer"], temperature=T)
         if c["mask_eos"]:
             eng.bias[EOS] = float("-inf")
         for t, v in c.get("bias_add", {}).items():
             eng.bias[int(t)] += v
         tokens = eng.generate(torch.from_numpy(frames), lens, c["max_new"]).clone().numpy()
+        torch.rand_like = rand_like
+        if T > 0:
+            assert drawn[0] == c["max_new"]
         bias = eng.bias.numpy().copy()
         rng = np.random.default_rng(c["frame_seed"] + 1000)
         tf_tokens = np.concatenate([np.ones((B, 1), np.int64),
@@ -93,9 +118,11 @@ def run_case(name, c, viktor):
     meta = dict(name=name, k=c["k"], cfg=cfg_kw, d_enc=d_enc, lens=lens, max_new=c["max_new"],
                 mask_eos=c["mask_eos"], max_homopolymer=c["max_homopolymer"], pos_scale=c.get("pos_scale", 1),
                 bias_add=c.get("bias_add", {}), weight_seed=c["weight_seed"], frame_seed=c["frame_seed"],
-                init="torch")
+                init="torch", temperature=T)
     arrays = dict(tokens=tokens, tf_logits=tf_logits.astype(np.float32), tf_tokens=tf_tokens,
                   bias=bias.astype(np.float32), meta=np.array(json.dumps(meta)))
+    if noise is not None:
+        arrays["noise"] = noise
     if c.get("store_weights"):
         arrays.update({"w:" + n: a for n, a in weights.items()})
     np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **arrays)

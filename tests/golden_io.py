@@ -9,7 +9,9 @@ from viktor_b200.config import DecoderConfig
 from viktor_b200.synthetic import make_frames, make_weights
 
 HERE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-CASES = ["base_theta1e6", "base_theta1e4", "kmer4", "homopolymer", "pos_scale2", "base_b8", "tiny"]
+CASES = ["base_theta1e6", "base_theta1e4", "kmer4", "homopolymer", "pos_scale2", "base_b8", "tiny", "sampled_t07",
+         "sampled_kmer4"]
+SAMPLED = ["sampled_t07", "sampled_kmer4"]
 
 
 def load(name):
@@ -21,5 +23,7 @@ def load(name):
     else:
         weights = make_weights(cfg, seed=meta["weight_seed"], init=meta["init"], d_enc=meta["d_enc"])
     frames = make_frames(meta["lens"], d_enc=meta["d_enc"], seed=meta["frame_seed"])
+    meta.setdefault("temperature", 0.0)
     return dict(meta=meta, cfg=cfg, weights=weights, frames=frames, tokens=z["tokens"],
-                tf_logits=z["tf_logits"], tf_tokens=z["tf_tokens"], bias=z["bias"])
+                tf_logits=z["tf_logits"], tf_tokens=z["tf_tokens"], bias=z["bias"],
+                noise=z["noise"] if "noise" in z.files else None)

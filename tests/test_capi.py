@@ -42,3 +42,13 @@ def test_argument_errors_are_status_codes():
     assert lib.vk_linear(None, None, None, 4, 64, 512, 0, 0, None) == _lib.VK_ERR_ARG
     assert lib.vk_decode_attention(None, None, None, None, None, 4, 0, 4, 100, 12800, 128, None, 0,
                                    None) == _lib.VK_ERR_ARG
+    # sampling needs the noise buffer and a positive, finite temperature
+    fake = 16  # any non-null address: validation fails before anything is dereferenced
+    ptrs = [fake] * 6  # tok, run, pos, plen, rope_off, out
+    assert lib.vk_sample_update(fake, 7, fake, fake, fake, 0, *ptrs, 4, 4, fake, fake, fake, 2, 7, 2, 0, None,
+                                None, None, None, 7, 0.7, None) == _lib.VK_ERR_ARG
+    for t in (0.0, -1.0, float("inf"), float("nan")):
+        assert lib.vk_sample_update(fake, 7, fake, fake, fake, 0, *ptrs, 4, 4, fake, fake, fake, 2, 7, 2, 0, None,
+                                    None, None, fake, 7, t, None) == _lib.VK_ERR_ARG
+    assert lib.vk_sample_update(fake, 7, fake, fake, fake, 0, *ptrs, 4, 4, fake, fake, fake, 2, 7, 2, 0, None,
+                                None, None, fake, 6, 0.7, None) == _lib.VK_ERR_ARG  # ld_noise < V

@@ -27,8 +27,9 @@ def test_oracle_greedy_tokens_match_reference(name):
     g = load(name)
     m = g["meta"]
     om = oracle_for(g)
+    noise = None if g["noise"] is None else (lambda i: g["noise"][i])
     out, margin = om.generate(g["frames"], m["lens"], m["max_new"], steps=m["max_new"], bias=g["bias"],
-                              max_homopolymer=m["max_homopolymer"])
+                              max_homopolymer=m["max_homopolymer"], temperature=m["temperature"], noise=noise)
     np.testing.assert_array_equal(out, g["tokens"])
     # every decided token had a clear fp32 margin, so the comparison is meaningful
     assert np.nanmin(margin) > 1e-4
@@ -56,8 +57,8 @@ def test_torch_cpu_baseline_port_matches_reference(name):
     from oracle.decoder_torch import TorchCPUModel
     g = load(name)
     m = g["meta"]
-    if m["pos_scale"] != 1:
-        pytest.skip("the timed port covers pos_scale 1")
+    if m["pos_scale"] != 1 or m["temperature"] > 0:
+        pytest.skip("the timed port covers pos_scale 1, greedy")
     tm = TorchCPUModel(OracleConfig(**m["cfg"]), g["weights"], k=m["k"])
     out = tm.generate(g["frames"], m["lens"], m["max_new"], g["bias"], m["max_homopolymer"])
     np.testing.assert_array_equal(out, g["tokens"])

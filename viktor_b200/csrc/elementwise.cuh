@@ -190,6 +190,10 @@ struct GreedyArgs {
   const __nv_bfloat16* emb;
   __nv_bfloat16* x;
   float* ssq;
+  // optional sampling (temperature > 0): uniform [0, 1) draws [B, V] (row stride ld_noise)
+  const float* noise;
+  int64_t ld_noise;
+  float temperature;
 };
 
 template <int D>
@@ -214,7 +218,11 @@ __global__ void __launch_bounds__(128) greedy_kernel(GreedyArgs a) {
   float best = -INFINITY;
   int bi = 0x7fffffff;
   for (int v = tid; v < a.V; v += 128) {
-    const float z = a.logits[static_cast<int64_t>(b) * a.ld_logits + v] + a.bias[v];
+    float z = a.logits[static_cast<int64_t>(b) * a.ld_logits + v] + a.bias[v];
+    if (a.noise) {  // Gumbel-max sampling, op for op as viktor/engine.py:81-82 (fp32 division and logarithms)
+      const float u = fmaxf(a.noise[static_cast<int64_t>(b) * a.ld_noise + v], 1e-20f);
+      z = z / a.temperature - logf(-logf(u));
+    }
     if (z > best || (z == best && v < bi)) {
       best = z;
       bi = v;

@@ -309,6 +309,52 @@ int vk_greedy_update(const float* logits, int64_t ld_logits, const float* bias, 
   a.emb = static_cast<const __nv_bfloat16*>(emb);
   a.x = static_cast<__nv_bfloat16*>(emb ? x : nullptr);
   a.ssq = ssq;
+  a.noise = nullptr;
+  a.ld_noise = 0;
+  a.temperature = 1.f;
+  return launch(ew::greedy_kernel<512>, dim3(B), dim3(128), 0, stream, 1, a);
+}
+
+int vk_sample_update(const float* logits, int64_t ld_logits, const float* bias, const uint8_t* is_tail,
+                     const uint8_t* is_homo, int homo_stop, int64_t* tok, int64_t* run, int64_t* pos,
+                     const int64_t* plen, const int64_t* rope_off, int64_t* out, int64_t out_stride,
+                     int64_t out_cols, int32_t* pos32, int32_t* seqlens, int32_t* rpos32, int B, int V, int eos,
+                     int pad, const void* emb, void* x, float* ssq, const float* noise, int64_t ld_noise,
+                     float temperature, void* stream) {
+  if (B == 0) return VK_OK;
+  if (B < 0 || V <= 0 || !logits || !bias || !is_tail || !is_homo || !tok || !run || !pos || !plen || !rope_off ||
+      !out || !pos32 || !seqlens || !rpos32 || !noise || ld_noise < V || !(temperature > 0.f) ||
+      !(temperature < INFINITY))
+    return VK_ERR_ARG;
+  if (emb && (!x || !ssq)) return VK_ERR_ARG;
+  ew::GreedyArgs a;
+  a.logits = logits;
+  a.ld_logits = ld_logits;
+  a.bias = bias;
+  a.is_tail = is_tail;
+  a.is_homo = is_homo;
+  a.homo_stop = homo_stop;
+  a.tok = tok;
+  a.run = run;
+  a.pos = pos;
+  a.plen = plen;
+  a.rope_off = rope_off;
+  a.out = out;
+  a.out_stride = out_stride;
+  a.out_cols = out_cols;
+  a.pos32 = pos32;
+  a.seqlens = seqlens;
+  a.rpos32 = rpos32;
+  a.B = B;
+  a.V = V;
+  a.eos = eos;
+  a.pad = pad;
+  a.emb = static_cast<const __nv_bfloat16*>(emb);
+  a.x = static_cast<__nv_bfloat16*>(emb ? x : nullptr);
+  a.ssq = ssq;
+  a.noise = noise;
+  a.ld_noise = ld_noise;
+  a.temperature = temperature;
   return launch(ew::greedy_kernel<512>, dim3(B), dim3(128), 0, stream, 1, a);
 }
 

@@ -75,11 +75,9 @@ class DecodeEngine:
             raise ValueError(f"backend {backend!r}: this engine runs the B200 CUDA kernels only")
         if attention_backend not in ("auto", "cuda", "triton", "flash"):
             raise ValueError(f"unknown decode attention backend: {attention_backend}")
-        if temperature != 0:
-            raise NotImplementedError("sampled decoding (temperature > 0) is not implemented; greedy only")
         load()
         self.model, self.dec = model, model.decoder
-        self.temperature = temperature
+        self.temperature = float(temperature)
         if device is None:
             dev = model.decoder.lm_head.weight.device
             device = dev if dev.type == "cuda" else torch.device("cuda", torch.cuda.current_device())
@@ -127,6 +125,10 @@ class DecodeEngine:
         self.logits = torch.zeros(B, self.w.vpad, dtype=torch.float32, device=dev)
         ws_bytes = load().vk_decode_attention_workspace_bytes(B, max_len)
         self.attn_ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+        # Sampled decoding (viktor/engine.py:81-82): one [B, V] draw of uniform noise per selection, made with
+        # the same generator call as the reference's torch.rand_like (captured into the step's graph).
+        self.noise = (torch.empty(B, self.w.vocab, dtype=torch.float32, device=dev) if self.temperature > 0
+                      else None)
         # Decode groups: the batch is split into row ranges whose steps run on their own streams, so that one
         # group's latency-bound projection chain overlaps another group's bandwidth-bound attention.  Every row
         # is computed exactly as in a single group (the split changes no arithmetic).
@@ -149,8 +151,15 @@ class DecodeEngine:
     def _stream(self):
         return torch.cuda.current_stream(self.device).cuda_stream
 
+    def _draw_noise(self):
+        """The uniform draws of one selection (torch.rand_like of viktor/engine.py:82: same shape, dtype and
+        generator call)."""
+        self.noise.uniform_()
+
     def _step(self):
-        """One greedy step for every sequence (viktor/engine.py:91-97, fused branch)."""
+        """One greedy (or sampled) step for every sequence (viktor/engine.py:91-116)."""
+        if self.noise is not None:
+            self._draw_noise()
         if not self._side_streams:
             lo, hi, ws = self._groups[0]
             self._step_rows(lo, hi, ws, self._stream())
@@ -179,11 +188,14 @@ class DecodeEngine:
         r = slice(lo, hi)
         logits = self.logits[r]
         self.fast.logits(x, ssq, logits, st)
-        call("vk_greedy_update", _p(logits), logits.stride(0), _p(self.bias), _p(self.is_tail), _p(self.is_homo),
-             self.homo_stop, _p(self.tok[r]), _p(self.run[r]), _p(self.pos[r]), _p(self.plen[r]),
-             _p(self.rope_off[r]), _p(self.out[r]), self.out.stride(0), self.out.shape[1], _p(self.pos32[r]),
-             _p(self.seqlens[r]), _p(self.rpos32[r]), hi - lo, w.vocab, EOS, PAD, _p(w.embed), _p(self.x[r]),
-             _p(self.ssq[r]), st)
+        args = (_p(logits), logits.stride(0), _p(self.bias), _p(self.is_tail), _p(self.is_homo), self.homo_stop,
+                _p(self.tok[r]), _p(self.run[r]), _p(self.pos[r]), _p(self.plen[r]), _p(self.rope_off[r]),
+                _p(self.out[r]), self.out.stride(0), self.out.shape[1], _p(self.pos32[r]), _p(self.seqlens[r]),
+                _p(self.rpos32[r]), hi - lo, w.vocab, EOS, PAD, _p(w.embed), _p(self.x[r]), _p(self.ssq[r]))
+        if self.noise is None:
+            call("vk_greedy_update", *args, st)
+        else:
+            call("vk_sample_update", *args, _p(self.noise[r]), self.noise.stride(0), self.temperature, st)
 
     @torch.no_grad()
     def _capture(self):
@@ -313,6 +325,8 @@ class DecodeEngine:
         self.plen.copy_(torch.tensor(frame_lens, device=self.device))
         self.pos.copy_(self.plen)
         self.rope_off.copy_(self.plen * (self.pos_scale - 1))
+        if self.noise is not None:
+            self._draw_noise()
         self._head_select(xcat, scat, st)
 
     # ------------------------------------------------------------------ decode loop
