@@ -191,6 +191,16 @@ int vk_gather_rows(const void* src, const int64_t* idx, void* dst, int64_t n, in
  * identity.  Indices are i64 and bounds-checked against src_rows / dst_rows. */
 int vk_copy_rows(const void* src, const int64_t* src_idx, int64_t src_rows, void* dst, const int64_t* dst_idx,
                  int64_t dst_rows, int64_t n, int row_bytes, void* stream);
+/* The packed prefill layout of viktor/engine.py:145-159, built on the device from the prefix lengths of one
+ * sub-batch (lens [n] i32 on the device, 1 <= n <= 4096; total = sum(lens) + n, known to the caller).
+ * Sequence b occupies packed rows cu[b] .. cu[b+1]-1: its lens[b] frames, then BOS.  Writes cu [n+1] i32,
+ * frame_idx [sum(lens)] i32 (packed row of each frame; NULL allowed when there are no frames), last [n] i64
+ * (BOS rows), pos / seq [total] i32 (position in the sequence, cache row row0 + b), rpos [total] i32
+ * (pos * pos_scale; NULL to skip) and lengths [n] i32 (lens + 1).  If the lengths do not add up to total (or
+ * one is negative) nothing is written and the device error word records a range error. */
+int vk_prefill_plan(const int32_t* lens, int n, int row0, int pos_scale, int64_t total, int32_t* cu,
+                    int32_t* frame_idx, int64_t* last, int32_t* pos, int32_t* seq, int32_t* rpos, int32_t* lengths,
+                    void* stream);
 /* x[rows[i], :] = emb[token, :] (d bf16 values per row). */
 int vk_scatter_embed(void* x, const int64_t* rows, int64_t n, int64_t x_rows, const void* emb, int64_t token,
                      int d, void* stream);

@@ -401,5 +401,92 @@ __global__ void scatter_embed_kernel(__nv_bfloat16* x, const int64_t* rows, int6
     *reinterpret_cast<uint4*>(x + dr * D + c) = *reinterpret_cast<const uint4*>(emb + token * D + c);
 }
 
+// ---- packed prefill plan (viktor/engine.py:145-159), built on the device from the prefix lengths ----------
+// Sequence b occupies packed rows cu[b] .. cu[b+1]-1: its lens[b] frames, then BOS.  Every CTA scans the n
+// lengths itself (n is a sub-batch, at most kPlanMaxSeq), then the grid strides over the packed rows.
+constexpr int kPlanMaxSeq = 4096;
+constexpr int kPlanThreads = 256;
+
+struct PlanArgs {
+  const int32_t* lens;   // [n]
+  int n, row0, pos_scale;
+  int64_t total;         // sum(lens) + n, as the caller sized the outputs
+  int32_t* cu;           // [n + 1]
+  int32_t* frame_idx;    // [sum(lens)]: packed row of each frame (may be null when there are no frames)
+  int64_t* last;         // [n]: packed row of each BOS
+  int32_t* pos;          // [total]: position inside the sequence
+  int32_t* seq;          // [total]: cache row (row0 + b)
+  int32_t* rpos;         // [total] RoPE position pos * pos_scale, or null
+  int32_t* lengths;      // [n]: lens + 1
+};
+
+__global__ void __launch_bounds__(kPlanThreads) prefill_plan_kernel(PlanArgs a) {
+  __shared__ int64_t scu[kPlanMaxSeq + 1];
+  __shared__ int64_t warp_tot[kPlanThreads / 32];
+  __shared__ int bad;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_wait();
+  if (tid == 0) bad = 0;
+  __syncthreads();
+  // exclusive scan of (lens + 1): each thread owns kPer consecutive sequences
+  constexpr int kPer = kPlanMaxSeq / kPlanThreads;
+  int64_t local[kPer];
+  int64_t sum = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int b = tid * kPer + i;
+    int64_t v = 0;
+    if (b < a.n) {
+      const int L = a.lens[b];
+      if (L < 0) bad = 1;
+      v = static_cast<int64_t>(L < 0 ? 0 : L) + 1;
+    }
+    local[i] = sum;
+    sum += v;
+  }
+  int64_t incl = sum;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int64_t o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += o;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  int64_t base = incl - sum;
+  for (int w = 0; w < warp; ++w) base += warp_tot[w];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int b = tid * kPer + i;
+    if (b <= a.n) scu[b] = base + local[i];
+  }
+  if (tid == kPlanThreads - 1 && a.n == kPlanMaxSeq) scu[kPlanMaxSeq] = base + sum;  // no thread starts there
+  __syncthreads();
+  if (scu[a.n] != a.total || bad) {  // the caller's sizes disagree with the lengths: write nothing
+    if (blockIdx.x == 0 && tid == 0) raise_error(ERR_BOUNDS);
+    return;
+  }
+  if (blockIdx.x == 0) {
+    for (int b = tid; b <= a.n; b += kPlanThreads) a.cu[b] = static_cast<int32_t>(scu[b]);
+    for (int b = tid; b < a.n; b += kPlanThreads) {
+      a.last[b] = scu[b + 1] - 1;
+      a.lengths[b] = static_cast<int32_t>(scu[b + 1] - scu[b]);
+    }
+  }
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * kPlanThreads + tid; t < a.total;
+       t += static_cast<int64_t>(gridDim.x) * kPlanThreads) {
+    int lo = 0, hi = a.n - 1;  // last b with scu[b] <= t
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (scu[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    const int b = lo;
+    const int p = static_cast<int>(t - scu[b]);
+    a.pos[t] = p;
+    a.seq[t] = a.row0 + b;
+    if (a.rpos) a.rpos[t] = p * a.pos_scale;
+    if (t < scu[b + 1] - 1 && a.frame_idx) a.frame_idx[scu[b] - b + p] = static_cast<int32_t>(t);
+  }
+}
+
 }  // namespace ew
 }  // namespace vk

@@ -315,6 +315,32 @@ int vk_greedy_update(const float* logits, int64_t ld_logits, const float* bias, 
   return launch(ew::greedy_kernel<512>, dim3(B), dim3(128), 0, stream, 1, a);
 }
 
+int vk_prefill_plan(const int32_t* lens, int n, int row0, int pos_scale, int64_t total, int32_t* cu,
+                    int32_t* frame_idx, int64_t* last, int32_t* pos, int32_t* seq, int32_t* rpos, int32_t* lengths,
+                    void* stream) {
+  if (n <= 0 || n > ew::kPlanMaxSeq || row0 < 0 || pos_scale < 1 || total < n || total > (int64_t(1) << 31) - 1 ||
+      !lens || !cu || !last || !pos || !seq || !lengths || (total > n && !frame_idx))
+    return VK_ERR_ARG;
+  ew::PlanArgs a;
+  a.lens = lens;
+  a.n = n;
+  a.row0 = row0;
+  a.pos_scale = pos_scale;
+  a.total = total;
+  a.cu = cu;
+  a.frame_idx = frame_idx;
+  a.last = last;
+  a.pos = pos;
+  a.seq = seq;
+  a.rpos = rpos;
+  a.lengths = lengths;
+  const int sms = device_sm_count();
+  if (sms <= 0) return VK_ERR_CUDA;
+  const int64_t want = (total + ew::kPlanThreads - 1) / ew::kPlanThreads;
+  const unsigned grid = static_cast<unsigned>(want < 2 * sms ? want : 2 * sms);
+  return launch(ew::prefill_plan_kernel, dim3(grid), dim3(ew::kPlanThreads), 0, stream, 1, a);
+}
+
 int vk_sample_update(const float* logits, int64_t ld_logits, const float* bias, const uint8_t* is_tail,
                      const uint8_t* is_homo, int homo_stop, int64_t* tok, int64_t* run, int64_t* pos,
                      const int64_t* plen, const int64_t* rope_off, int64_t* out, int64_t out_stride,

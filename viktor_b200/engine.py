@@ -228,18 +228,25 @@ class DecodeEngine:
 
     # ------------------------------------------------------------------ prefill
     def _plan(self, lens, row0):
-        """Packed layout of one sub-batch, built on the host once per length tuple and kept on the device."""
+        """Packed layout of one sub-batch (viktor/engine.py:145-159), built on the device by vk_prefill_plan from
+        the n prefix lengths (one small host->device copy) once per length tuple and kept on the device."""
         key = tuple(lens)
         entry = self._prefill_plans.get(row0)
         if entry is not None and entry[0] == key:
             return entry[1]
-        a = prefill_plan(lens, row0, self.pos_scale)
-        dev = self.device
-
-        def t(x):
-            return None if x is None else torch.from_numpy(np.ascontiguousarray(x)).to(dev)
-
-        plan = {k: t(v) if isinstance(v, np.ndarray) else v for k, v in a.items()}
+        dev, n = self.device, len(lens)
+        frames = int(sum(lens))
+        total = frames + n
+        i32 = dict(dtype=torch.int32, device=dev)
+        plan = dict(cu=torch.empty(n + 1, **i32), frame_idx=torch.empty(max(frames, 1), **i32)[:frames],
+                    last=torch.empty(n, dtype=torch.int64, device=dev), pos=torch.empty(total, **i32),
+                    seq=torch.empty(total, **i32), rpos=None if self.pos_scale == 1 else torch.empty(total, **i32),
+                    lengths=torch.empty(n, **i32), total=total, frames=frames, max_len=max(lens) + 1, n=n)
+        lens_d = torch.tensor(lens, dtype=torch.int32).to(dev, non_blocking=True)
+        call("vk_prefill_plan", _p(lens_d), n, row0, self.pos_scale, total, _p(plan["cu"]), _p(plan["frame_idx"]),
+             _p(plan["last"]), _p(plan["pos"]), _p(plan["seq"]), None if plan["rpos"] is None else _p(plan["rpos"]),
+             _p(plan["lengths"]), self._stream())
+        plan["_lens"] = lens_d  # keeps the source alive until the plan kernel has run
         self._prefill_plans[row0] = (key, plan)
         return plan
 
