@@ -278,8 +278,8 @@ def test_decode_attention_ignores_stale_rows_and_row_offset():
 def test_prefill_attention():
     from viktor_b200.ops import prefill_attention
     torch.manual_seed(3)
-    lens = [1, 63, 64, 65, 200, 777, 2049]
-    S, R, row0 = 2100, 10, 2
+    lens = [1, 63, 64, 65, 127, 128, 129, 200, 256, 777, 2049]
+    S, R, row0 = 2100, 14, 2
     n = sum(lens)
     cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=DEV)
     q = torch.randn(n, 8, 64, device=DEV, dtype=BF)

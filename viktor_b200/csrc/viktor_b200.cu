@@ -393,11 +393,12 @@ size_t vk_decode_attention_workspace_bytes(int nq, int S) {
   return counters + ml + o;
 }
 
+// TMA maps of one layer of the KV cache, [rows][S][2 heads][64] bf16: boxes of box_pos positions x one head.
 static bool make_cache_maps(CUtensorMap* mk, CUtensorMap* mv, const void* k, const void* v, int cache_rows, int S,
-                            int64_t stride_kb, int64_t stride_ks) {
+                            int64_t stride_kb, int64_t stride_ks, uint32_t box_pos = 64) {
   uint64_t dims[4] = {64, 2, static_cast<uint64_t>(S), static_cast<uint64_t>(cache_rows)};
   uint64_t strides[3] = {128, static_cast<uint64_t>(stride_ks) * 2, static_cast<uint64_t>(stride_kb) * 2};
-  uint32_t box[4] = {64, 1, 64, 1};
+  uint32_t box[4] = {64, 1, box_pos, 1};
   return make_map_bf16(mk, k, 4, dims, strides, box, true) && make_map_bf16(mv, v, 4, dims, strides, box, true);
 }
 
@@ -499,15 +500,16 @@ int vk_prefill_attention(const void* q, const void* k_cache, const void* v_cache
   {
     uint64_t dims[3] = {64, 8, static_cast<uint64_t>(n_tok)};
     uint64_t strides[2] = {128, 1024};
-    uint32_t box[3] = {64, 1, 64};
+    uint32_t box[3] = {64, 1, pattn::kBQ};
     if (!make_map_bf16(&mq, q, 3, dims, strides, box, true)) return VK_ERR_ARG;
   }
-  if (!make_cache_maps(&mk, &mv, k_cache, v_cache, cache_rows, S, stride_kb, stride_ks)) return VK_ERR_ARG;
+  if (!make_cache_maps(&mk, &mv, k_cache, v_cache, cache_rows, S, stride_kb, stride_ks, pattn::kBK))
+    return VK_ERR_ARG;
   pattn::PrefillArgs a;
   a.cu_seqlens = cu_seqlens;
   a.nseq = nseq;
   a.row0 = row0;
-  a.n_qtiles = (max_seqlen + 63) / 64;
+  a.n_qtiles = (max_seqlen + pattn::kBQ - 1) / pattn::kBQ;
   a.S = S;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.scale_log2 = 0.125f * 1.4426950408889634f;
