@@ -1,7 +1,8 @@
 """End-to-end parity of the B200 engine against the reference (golden fixtures) and the CPU oracle.
 
 * Teacher-forced logits (all layers over [frames | tokens]) agree with the reference's fp32 logits within
-  max-abs 3e-2 (bf16 storage between ops, the same rounding points as the reference's Triton path).
+  max-abs 2.5e-2 (bf16 storage between ops, the same rounding points as the reference's Triton path;
+  measured 0.015-0.017 for the 7-token vocabulary, 0.022 for the 343-token 4-mer head).
 * Greedy tokens equal the reference's, per chunk, up to the first step whose fp32 top-2 logit margin is below
   the bf16 noise floor (0.05); from there on a bf16 path may legitimately pick the other token.
 * The CUDA-graph decode equals the eager decode token for token.
@@ -64,7 +65,8 @@ def test_teacher_forced_logits_match_reference(name):
     got = eng.teacher_forced_logits(torch.from_numpy(g["frames"]), m["lens"],
                                     torch.from_numpy(g["tf_tokens"])).cpu().numpy()
     err = np.abs(got - g["tf_logits"]).max()
-    assert err < 3e-2, f"max |logits - reference fp32| = {err}"
+    print(f"{name}: max |logits - reference fp32| = {err:.4f}")
+    assert err < 2.5e-2, f"max |logits - reference fp32| = {err}"
 
 
 @pytest.mark.parametrize("name", CASES)
@@ -142,3 +144,31 @@ def test_full_size_matches_oracle_on_samples(full_size):
     ref, margin = om.generate(sub, [2048] * len(pick), f["steps"], steps=f["steps"], bias=bias, max_homopolymer=None)
     ok = agree_until_low_margin(f["out"][pick], ref, margin)
     assert ok.all(), f"\n{f['out'][pick]}\n{ref}\n{margin}"
+
+
+def test_greedy_chunks_identical_to_oracle_rate():
+    """128 chunks of 64..512 frames, 32 greedy steps against the fp32 oracle (which reproduces the reference's
+    tokens on every golden case).  Every chunk agrees up to its first step whose fp32 top-2 margin is below the
+    bf16 noise floor; with this random (untrained) init such near-ties occur in a few chunks within 32 steps,
+    so the fraction of chunks identical over all steps is measured (0.969 on B200) and held above 0.95."""
+    from viktor_b200 import Basecaller, DecodeEngine, DecoderConfig
+    from viktor_b200.synthetic import make_frames, make_weights
+    cfg = DecoderConfig(vocab_size=7, rope_theta=1e6)
+    weights = make_weights(cfg, seed=31, init="torch")
+    rng = np.random.default_rng(32)
+    lens = [int(v) for v in rng.integers(64, 513, 128)]
+    frames = make_frames(lens, seed=33)
+    steps = 32
+    model = Basecaller.from_weights(weights, k=1, cfg=cfg)
+    eng = DecodeEngine(model, len(lens), steps, max(lens), max_homopolymer=None, device="cuda")
+    eng.bias[2] = float("-inf")
+    got = eng.generate(torch.from_numpy(frames), lens, steps).cpu().numpy()
+    bias = np.zeros(7, np.float32)
+    bias[[0, 1, 2]] = -np.inf
+    om = OracleModel(OracleConfig(vocab_size=7, rope_theta=1e6), weights, k=1)
+    ref, margin = om.generate(frames, lens, steps, steps=steps, bias=bias, max_homopolymer=None)
+    ok = agree_until_low_margin(got, ref, margin)
+    exact = (got == ref).all(1).mean()
+    print(f"identical chunks {exact:.4f} ({(got == ref).all(1).sum()} / {len(lens)})")
+    assert ok.all(), np.where(~ok)[0]
+    assert exact >= 0.95
