@@ -13,7 +13,7 @@
 //                                   an MN-major operand straight from its TMA tile -> TMEM O (fp32)
 //   warps 2-5   softmax, one query row per thread (TMEM lane = row): the score row in one TMEM round trip,
 //               row max, exp2, P_j rounded to bf16 into TMEM, and the FlashAttention rescale of the TMEM
-//               accumulator (O *= alpha, skipped by a warp whose rows' maxima did not move) before O += P_j V_j.
+//               accumulator (O *= alpha, lazily: only when a row's reference maximum moved) before O += P_j V_j.
 // S_{j+1} is computed while the softmax warps work on tile j.  TMEM holds S (128 columns), P (64) and O (64):
 // 256 columns, so two CTAs share an SM.  The causal mask only touches the diagonal tile.  P is rounded to
 // bf16 before P.V and the row sums use the unrounded fp32 probabilities, as the FlashAttention-2 kernel the
@@ -198,13 +198,25 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free);
-      float mx = -INFINITY;
+      // row max of the raw scores (the scale is positive); the causal mask only on the diagonal tile
+      if (diag) {
 #pragma unroll
-      for (int i = 0; i < kBK; ++i) {
-        v[i] = (diag && key0 + i > qpos) ? -INFINITY : v[i] * a.scale_log2;
-        mx = fmaxf(mx, v[i]);
+        for (int i = 0; i < kBK; ++i)
+          if (key0 + i > qpos) v[i] = -INFINITY;
       }
-      const float m_new = fmaxf(m, mx);
+      float mx8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx8[k] = v[k];
+#pragma unroll
+      for (int i = 8; i < kBK; i += 8)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], v[i + k]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * a.scale_log2;
+      // Lazy rescale: the exponentials keep using the row's current reference maximum m unless the tile's
+      // maximum exceeds it by more than 8 (log2 units); then probabilities stay below 2^8, exact in fp32 and
+      // bf16-rounded with the same relative error, and most tiles need no accumulator rescale.
+      const float m_new = (mx > m + 8.f || m == -INFINITY) ? fmaxf(m, mx) : m;
       const float mu = m_new == -INFINITY ? 0.f : m_new;
       const float alpha = exp2f(m - mu);
       // O += P_{j-1} V_{j-1} must have finished before P_j and the rescale overwrite P and O
@@ -216,19 +228,21 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tc_fence_after();
       }
-      // P_j (bf16) into TMEM, 32 keys per store
-      float rs = 0.f;
+      // P_j = exp2(s * scale - mu) (bf16) into TMEM, 32 keys per store; partial row sums for ILP
+      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c0 = 0; c0 < kBK; c0 += 32) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float p0 = exp2f(v[c0 + i] - mu), p1 = exp2f(v[c0 + i + 1] - mu);
-          rs += p0 + p1;
+          const float p0 = fast_exp2(fmaf(v[c0 + i], a.scale_log2, -mu));
+          const float p1 = fast_exp2(fmaf(v[c0 + i + 1], a.scale_log2, -mu));
+          rs8[(i >> 1) & 7] += p0 + p1;
           pk[i / 2] = pack_bf16x2(p0, p1);
         }
         tmem_st16(trow + kColP + c0 / 2, pk);
       }
+      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       // rescale the accumulator when this warp's row maxima moved (alpha = 1 otherwise)
       if (j >= 1 && !__all_sync(0xffffffffu, alpha == 1.f)) {
         float o[64];

@@ -40,6 +40,14 @@ VK_DEV uint64_t globaltimer() {
 // unrolled epilogue.
 VK_DEV float silu(float g) { return g * __fdividef(1.0f, 1.0f + __expf(-g)); }
 
+// 2^x with the hardware approximation (ex2.approx.ftz.f32: relative error ~2^-22, 2^-inf = 0), for softmax
+// probabilities that are rounded to bf16 right after.
+VK_DEV float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 VK_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
 // ---- mbarrier ---------------------------------------------------------------------------------------------
