@@ -133,9 +133,14 @@ VK_DEV float row_rscale(const EpiArgs& ep, int row) {
 
 // QK-RMSNorm + RoPE of one 64-wide head held by this thread (viktor/triton_ops.py:44-49).
 VK_DEV void norm_rope_head(float* v, const __nv_bfloat16* w, const float* c, const float* s, float eps) {
-  float ss = 0.f;
+  float ss8[8];  // eight independent chains: the 64-term sum is a latency chain otherwise
 #pragma unroll
-  for (int i = 0; i < 64; ++i) ss += v[i] * v[i];
+  for (int k = 0; k < 8; ++k) ss8[k] = v[k] * v[k];
+#pragma unroll
+  for (int i = 8; i < 64; i += 8)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss8[k] = fmaf(v[i + k], v[i + k], ss8[k]);
+  const float ss = ((ss8[0] + ss8[1]) + (ss8[2] + ss8[3])) + ((ss8[4] + ss8[5]) + (ss8[6] + ss8[7]));
   const float r = rsqrtf(ss * (1.0f / 64.0f) + eps);
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
@@ -207,7 +212,7 @@ VK_DEV void epi_chunk(const EpiArgs& ep, int row, int n_tile, int ch, float* v, 
   } else if (EPI == ADD_RESID) {
     const int c0 = n_tile * BN + ch * 64;
     __nv_bfloat16* xp = ep.x + static_cast<int64_t>(row) * N + c0;
-    float ss = 0.f;
+    float ss8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent chains (see norm_rope_head)
 #pragma unroll
     for (int i = 0; i < 64; i += 8) {
       float xo[8];
@@ -215,11 +220,12 @@ VK_DEV void epi_chunk(const EpiArgs& ep, int row, int n_tile, int ch, float* v, 
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         xo[e] = bf16_round(xo[e] + bf16_round(v[i + e]));
-        ss += xo[e] * xo[e];
+        ss8[e] = fmaf(xo[e], xo[e], ss8[e]);
       }
       store_bf16x8(xp + i, xo);
     }
-    ep.ssq_out[static_cast<int64_t>(row) * kSsqSlots + c0 / 64] = ss;
+    ep.ssq_out[static_cast<int64_t>(row) * kSsqSlots + c0 / 64] =
+        ((ss8[0] + ss8[1]) + (ss8[2] + ss8[3])) + ((ss8[4] + ss8[5]) + (ss8[6] + ss8[7]));
   } else if (EPI == QKV_ROPE) {
     const int H = ep.n_heads, HKV = ep.n_kv_heads;
     const int gh = n_tile * (BN / 64) + ch;
