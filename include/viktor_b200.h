@@ -191,6 +191,19 @@ int vk_gather_rows(const void* src, const int64_t* idx, void* dst, int64_t n, in
  * identity.  Indices are i64 and bounds-checked against src_rows / dst_rows. */
 int vk_copy_rows(const void* src, const int64_t* src_idx, int64_t src_rows, void* dst, const int64_t* dst_idx,
                  int64_t dst_rows, int64_t n, int row_bytes, void* stream);
+/* The decode head in one kernel: lm_head + selection + state advance + next embedding.  x_final [B, 512] bf16
+ * and ssq_final [B, 8] f32 are the final residual and its per-64-column sums of squares; head_w [V, 512] bf16
+ * is the lm_head with the final RMSNorm weight folded in (logits = rsqrt(mean(x^2) + eps) * x . head_w^T, fp32,
+ * as the fp32-output linear of viktor/engine.py:95-96); V <= 512.  The remaining arguments are those of
+ * vk_sample_update; noise = NULL selects greedily (vk_greedy_update).  x / ssq may alias x_final / ssq_final
+ * (each row is read before it is overwritten with the next token's embedding). */
+int vk_head_select(const void* x_final, const float* ssq_final, float eps, const void* head_w, const float* bias,
+                   const uint8_t* is_tail, const uint8_t* is_homo, int homo_stop, int64_t* tok, int64_t* run,
+                   int64_t* pos, const int64_t* plen, const int64_t* rope_off, int64_t* out, int64_t out_stride,
+                   int64_t out_cols, int32_t* pos32, int32_t* seqlens, int32_t* rpos32, int B, int V, int eos, int pad,
+                   const void* emb, void* x, float* ssq, const float* noise, int64_t ld_noise, float temperature,
+                   void* stream);
+
 /* The packed prefill layout of viktor/engine.py:145-159, built on the device from the prefix lengths of one
  * sub-batch (lens [n] i32 on the device, 1 <= n <= 4096; total = sum(lens) + n, known to the caller).
  * Sequence b occupies packed rows cu[b] .. cu[b+1]-1: its lens[b] frames, then BOS.  Writes cu [n+1] i32,

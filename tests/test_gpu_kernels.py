@@ -335,3 +335,51 @@ def test_greedy_update_grammar():
     assert torch.equal(x, emb[tok])
     ref_ssq = emb[tok].float().view(B, 8, 64).square().sum(-1)
     assert torch.allclose(ssq, ref_ssq, rtol=1e-5, atol=1e-4)
+
+
+def test_head_select_equals_lm_head_then_greedy():
+    """vk_head_select (lm_head with the folded final norm fused into the selection kernel) picks the tokens of
+    fp32 logits r * x . W^T followed by vk_greedy_update, and advances the same state, for both vocabularies."""
+    from viktor_b200._lib import call
+    from viktor_b200.config import KmerTokenizer
+    from viktor_b200.engine import _masks
+    for k, B in ((1, 64), (4, 48)):
+        tk = KmerTokenizer(k)
+        V = tk.vocab_size
+        g = torch.Generator(device="cuda").manual_seed(7 + k)
+        x = torch.randn(B, 512, generator=g, device=DEV).to(BF)
+        xf = x.float()
+        ssq = torch.stack([(xf[:, 64 * i:64 * (i + 1)] ** 2).sum(1) for i in range(8)], 1).contiguous()
+        w = (torch.randn(V, 512, generator=g, device=DEV) * 0.3).to(BF)
+        r = torch.rsqrt(ssq.sum(1, keepdim=True) / 512 + 1e-6)
+        logits = (xf @ w.float().t()) * r
+        bias = torch.zeros(V, device=DEV)
+        bias[:2] = float("-inf")
+        tail, homo = _masks(tk, torch.device(DEV))
+        emb = torch.randn(V, 512, generator=g, device=DEV).to(BF)
+        st = torch.cuda.current_stream().cuda_stream
+
+        def state():
+            return dict(tok=torch.randint(3, V, (B,), generator=g, device=DEV), run=torch.zeros(B, dtype=torch.long, device=DEV),
+                        pos=torch.full((B,), 10, dtype=torch.long, device=DEV), plen=torch.full((B,), 9, dtype=torch.long, device=DEV),
+                        roff=torch.zeros(B, dtype=torch.long, device=DEV), out=torch.zeros(B, 8, dtype=torch.long, device=DEV),
+                        p32=torch.zeros(B, dtype=torch.int32, device=DEV), sl=torch.zeros(B, dtype=torch.int32, device=DEV),
+                        rp=torch.zeros(B, dtype=torch.int32, device=DEV), x=torch.empty(B, 512, dtype=BF, device=DEV),
+                        ssq=torch.empty(B, 8, device=DEV))
+        s1 = state()
+        s2 = {key: v.clone() for key, v in s1.items()}
+        p = lambda t: t.data_ptr()
+        call("vk_greedy_update", p(logits), logits.stride(0), p(bias), p(tail), p(homo), 0, p(s1["tok"]), p(s1["run"]),
+             p(s1["pos"]), p(s1["plen"]), p(s1["roff"]), p(s1["out"]), 8, 8, p(s1["p32"]), p(s1["sl"]), p(s1["rp"]), B, V,
+             2, 0, p(emb), p(s1["x"]), p(s1["ssq"]), st)
+        call("vk_head_select", p(x), p(ssq), 1e-6, p(w), p(bias), p(tail), p(homo), 0, p(s2["tok"]), p(s2["run"]),
+             p(s2["pos"]), p(s2["plen"]), p(s2["roff"]), p(s2["out"]), 8, 8, p(s2["p32"]), p(s2["sl"]), p(s2["rp"]), B, V,
+             2, 0, p(emb), p(s2["x"]), p(s2["ssq"]), None, 0, 1.0, st)
+        torch.cuda.synchronize()
+        top2 = (logits + bias).topk(2, 1).values
+        clear = (top2[:, 0] - top2[:, 1]) > 1e-3
+        assert clear.float().mean() > 0.9
+        assert torch.equal(s1["tok"][clear], s2["tok"][clear])
+        for key in ("pos", "p32", "sl", "rp"):
+            assert torch.equal(s1[key], s2[key])
+        assert torch.equal(s1["x"][clear], s2["x"][clear])

@@ -194,18 +194,49 @@ struct GreedyArgs {
   const float* noise;
   int64_t ld_noise;
   float temperature;
+  // optional fused lm_head: logits = rsqrt(mean(x^2) + eps) * x . head_w^T from the final residual (head_w is
+  // the lm_head with the final norm folded in, [V, D] bf16); `logits` is then not read
+  const __nv_bfloat16* head_x;
+  const float* head_ssq;
+  const __nv_bfloat16* head_w;
+  float head_eps;
 };
+constexpr int kHeadMaxV = 512;  // vocabulary of the fused head (the 4-mer vocabulary has 343 tokens)
 
 template <int D>
 __global__ void __launch_bounds__(128) greedy_kernel(GreedyArgs a) {
   __shared__ float sv[4];
   __shared__ int si[4];
   __shared__ int64_t chosen;
+  __shared__ float slog[kHeadMaxV];
   const int b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_launch_dependents();
   pdl_wait();
   if (b >= a.B) return;
+  if (a.head_w) {
+    // logits of this row: lane j of every warp holds x[16j .. 16j + 15]; warp w computes tokens w, w + 4, ...
+    static_assert(D == 512, "fused head: 16 columns per lane");
+    float xv[16];
+    load8(a.head_x + static_cast<int64_t>(b) * D + lane * 16, xv);
+    load8(a.head_x + static_cast<int64_t>(b) * D + lane * 16 + 8, xv + 8);
+    const float4* sp = reinterpret_cast<const float4*>(a.head_ssq + static_cast<int64_t>(b) * 8);
+    const float4 s0 = sp[0], s1 = sp[1];
+    const float r = rsqrtf((((s0.x + s0.y) + (s0.z + s0.w)) + ((s1.x + s1.y) + (s1.z + s1.w))) * (1.0f / D) +
+                           a.head_eps);
+    for (int v = warp; v < a.V; v += 4) {
+      float wv[16];
+      load8(a.head_w + static_cast<int64_t>(v) * D + lane * 16, wv);
+      load8(a.head_w + static_cast<int64_t>(v) * D + lane * 16 + 8, wv + 8);
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc = fmaf(xv[i], wv[i], acc);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+      if (lane == 0) slog[v] = acc * r;
+    }
+    __syncthreads();
+  }
   // state of this sequence, loaded while the argmax runs
   int64_t prev = 0, run0 = 0, p = 0, pl = 0, roff = 0;
   if (tid == 0) {
@@ -218,7 +249,7 @@ __global__ void __launch_bounds__(128) greedy_kernel(GreedyArgs a) {
   float best = -INFINITY;
   int bi = 0x7fffffff;
   for (int v = tid; v < a.V; v += 128) {
-    float z = a.logits[static_cast<int64_t>(b) * a.ld_logits + v] + a.bias[v];
+    float z = (a.head_w ? slog[v] : a.logits[static_cast<int64_t>(b) * a.ld_logits + v]) + a.bias[v];
     if (a.noise) {  // Gumbel-max sampling, op for op as viktor/engine.py:81-82 (fp32 division and logarithms)
       const float u = fmaxf(a.noise[static_cast<int64_t>(b) * a.ld_noise + v], 1e-20f);
       z = z / a.temperature - logf(-logf(u));

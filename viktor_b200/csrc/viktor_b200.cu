@@ -274,17 +274,14 @@ int vk_swiglu(const void* gu, void* out, int64_t n, int F, void* stream) {
                 static_cast<const __nv_bfloat16*>(gu), static_cast<__nv_bfloat16*>(out), n, F);
 }
 
-int vk_greedy_update(const float* logits, int64_t ld_logits, const float* bias, const uint8_t* is_tail,
-                     const uint8_t* is_homo, int homo_stop, int64_t* tok, int64_t* run, int64_t* pos,
-                     const int64_t* plen, const int64_t* rope_off, int64_t* out, int64_t out_stride,
-                     int64_t out_cols, int32_t* pos32, int32_t* seqlens, int32_t* rpos32, int B, int V, int eos,
-                     int pad, const void* emb, void* x, float* ssq, void* stream) {
-  if (B == 0) return VK_OK;
-  if (B < 0 || V <= 0 || !logits || !bias || !is_tail || !is_homo || !tok || !run || !pos || !plen || !rope_off ||
-      !out || !pos32 || !seqlens || !rpos32)
-    return VK_ERR_ARG;
-  if (emb && (!x || !ssq)) return VK_ERR_ARG;
+// Fields shared by the selection entry points (viktor/triton_ops.py:172-209, viktor/engine.py:79-89).
+static ew::GreedyArgs greedy_args(const float* logits, int64_t ld_logits, const float* bias, const uint8_t* is_tail,
+                                  const uint8_t* is_homo, int homo_stop, int64_t* tok, int64_t* run, int64_t* pos,
+                                  const int64_t* plen, const int64_t* rope_off, int64_t* out, int64_t out_stride,
+                                  int64_t out_cols, int32_t* pos32, int32_t* seqlens, int32_t* rpos32, int B, int V,
+                                  int eos, int pad, const void* emb, void* x, float* ssq) {
   ew::GreedyArgs a;
+  memset(&a, 0, sizeof(a));
   a.logits = logits;
   a.ld_logits = ld_logits;
   a.bias = bias;
@@ -309,9 +306,30 @@ int vk_greedy_update(const float* logits, int64_t ld_logits, const float* bias, 
   a.emb = static_cast<const __nv_bfloat16*>(emb);
   a.x = static_cast<__nv_bfloat16*>(emb ? x : nullptr);
   a.ssq = ssq;
-  a.noise = nullptr;
-  a.ld_noise = 0;
   a.temperature = 1.f;
+  return a;
+}
+
+static bool greedy_state_ok(const float* bias, const uint8_t* is_tail, const uint8_t* is_homo, const int64_t* tok,
+                            const int64_t* run, const int64_t* pos, const int64_t* plen, const int64_t* rope_off,
+                            const int64_t* out, const int32_t* pos32, const int32_t* seqlens, const int32_t* rpos32,
+                            int B, int V, const void* emb, const void* x, const float* ssq) {
+  return B > 0 && V > 0 && bias && is_tail && is_homo && tok && run && pos && plen && rope_off && out && pos32 &&
+         seqlens && rpos32 && (!emb || (x && ssq));
+}
+
+int vk_greedy_update(const float* logits, int64_t ld_logits, const float* bias, const uint8_t* is_tail,
+                     const uint8_t* is_homo, int homo_stop, int64_t* tok, int64_t* run, int64_t* pos,
+                     const int64_t* plen, const int64_t* rope_off, int64_t* out, int64_t out_stride,
+                     int64_t out_cols, int32_t* pos32, int32_t* seqlens, int32_t* rpos32, int B, int V, int eos,
+                     int pad, const void* emb, void* x, float* ssq, void* stream) {
+  if (B == 0) return VK_OK;
+  if (!logits || !greedy_state_ok(bias, is_tail, is_homo, tok, run, pos, plen, rope_off, out, pos32, seqlens, rpos32,
+                                  B, V, emb, x, ssq))
+    return VK_ERR_ARG;
+  const ew::GreedyArgs a = greedy_args(logits, ld_logits, bias, is_tail, is_homo, homo_stop, tok, run, pos, plen,
+                                       rope_off, out, out_stride, out_cols, pos32, seqlens, rpos32, B, V, eos, pad,
+                                       emb, x, ssq);
   return launch(ew::greedy_kernel<512>, dim3(B), dim3(128), 0, stream, 1, a);
 }
 
@@ -348,39 +366,42 @@ int vk_sample_update(const float* logits, int64_t ld_logits, const float* bias, 
                      int pad, const void* emb, void* x, float* ssq, const float* noise, int64_t ld_noise,
                      float temperature, void* stream) {
   if (B == 0) return VK_OK;
-  if (B < 0 || V <= 0 || !logits || !bias || !is_tail || !is_homo || !tok || !run || !pos || !plen || !rope_off ||
-      !out || !pos32 || !seqlens || !rpos32 || !noise || ld_noise < V || !(temperature > 0.f) ||
-      !(temperature < INFINITY))
+  if (!logits || !greedy_state_ok(bias, is_tail, is_homo, tok, run, pos, plen, rope_off, out, pos32, seqlens, rpos32,
+                                  B, V, emb, x, ssq) ||
+      !noise || ld_noise < V || !(temperature > 0.f) || !(temperature < INFINITY))
     return VK_ERR_ARG;
-  if (emb && (!x || !ssq)) return VK_ERR_ARG;
-  ew::GreedyArgs a;
-  a.logits = logits;
-  a.ld_logits = ld_logits;
-  a.bias = bias;
-  a.is_tail = is_tail;
-  a.is_homo = is_homo;
-  a.homo_stop = homo_stop;
-  a.tok = tok;
-  a.run = run;
-  a.pos = pos;
-  a.plen = plen;
-  a.rope_off = rope_off;
-  a.out = out;
-  a.out_stride = out_stride;
-  a.out_cols = out_cols;
-  a.pos32 = pos32;
-  a.seqlens = seqlens;
-  a.rpos32 = rpos32;
-  a.B = B;
-  a.V = V;
-  a.eos = eos;
-  a.pad = pad;
-  a.emb = static_cast<const __nv_bfloat16*>(emb);
-  a.x = static_cast<__nv_bfloat16*>(emb ? x : nullptr);
-  a.ssq = ssq;
+  ew::GreedyArgs a = greedy_args(logits, ld_logits, bias, is_tail, is_homo, homo_stop, tok, run, pos, plen, rope_off,
+                                 out, out_stride, out_cols, pos32, seqlens, rpos32, B, V, eos, pad, emb, x, ssq);
   a.noise = noise;
   a.ld_noise = ld_noise;
   a.temperature = temperature;
+  return launch(ew::greedy_kernel<512>, dim3(B), dim3(128), 0, stream, 1, a);
+}
+
+int vk_head_select(const void* x_final, const float* ssq_final, float eps, const void* head_w, const float* bias,
+                   const uint8_t* is_tail, const uint8_t* is_homo, int homo_stop, int64_t* tok, int64_t* run,
+                   int64_t* pos, const int64_t* plen, const int64_t* rope_off, int64_t* out, int64_t out_stride,
+                   int64_t out_cols, int32_t* pos32, int32_t* seqlens, int32_t* rpos32, int B, int V, int eos, int pad,
+                   const void* emb, void* x, float* ssq, const float* noise, int64_t ld_noise, float temperature,
+                   void* stream) {
+  if (B == 0) return VK_OK;
+  if (!x_final || !ssq_final || !head_w || V > ew::kHeadMaxV || !aligned16(x_final) || !aligned16(ssq_final) ||
+      !aligned16(head_w) ||
+      !greedy_state_ok(bias, is_tail, is_homo, tok, run, pos, plen, rope_off, out, pos32, seqlens, rpos32, B, V, emb,
+                       x, ssq))
+    return VK_ERR_ARG;
+  if (noise && (ld_noise < V || !(temperature > 0.f) || !(temperature < INFINITY))) return VK_ERR_ARG;
+  ew::GreedyArgs a = greedy_args(nullptr, 0, bias, is_tail, is_homo, homo_stop, tok, run, pos, plen, rope_off, out,
+                                 out_stride, out_cols, pos32, seqlens, rpos32, B, V, eos, pad, emb, x, ssq);
+  a.head_x = static_cast<const __nv_bfloat16*>(x_final);
+  a.head_ssq = ssq_final;
+  a.head_w = static_cast<const __nv_bfloat16*>(head_w);
+  a.head_eps = eps;
+  if (noise) {
+    a.noise = noise;
+    a.ld_noise = ld_noise;
+    a.temperature = temperature;
+  }
   return launch(ew::greedy_kernel<512>, dim3(B), dim3(128), 0, stream, 1, a);
 }
 

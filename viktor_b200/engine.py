@@ -186,16 +186,14 @@ class DecodeEngine:
         w = self.w
         hi = self.B if hi is None else hi
         r = slice(lo, hi)
-        logits = self.logits[r]
-        self.fast.logits(x, ssq, logits, st)
-        args = (_p(logits), logits.stride(0), _p(self.bias), _p(self.is_tail), _p(self.is_homo), self.homo_stop,
-                _p(self.tok[r]), _p(self.run[r]), _p(self.pos[r]), _p(self.plen[r]), _p(self.rope_off[r]),
-                _p(self.out[r]), self.out.stride(0), self.out.shape[1], _p(self.pos32[r]), _p(self.seqlens[r]),
-                _p(self.rpos32[r]), hi - lo, w.vocab, EOS, PAD, _p(w.embed), _p(self.x[r]), _p(self.ssq[r]))
-        if self.noise is None:
-            call("vk_greedy_update", *args, st)
-        else:
-            call("vk_sample_update", *args, _p(self.noise[r]), self.noise.stride(0), self.temperature, st)
+        # lm_head (final norm folded in) fused into the selection kernel, which also writes the next step's
+        # embedding into self.x (x may be those same rows: each is read before it is overwritten)
+        noise = (None, 0, 1.0) if self.noise is None else (_p(self.noise[r]), self.noise.stride(0), self.temperature)
+        call("vk_head_select", _p(x), _p(ssq), w.eps, _p(w.lm_head), _p(self.bias), _p(self.is_tail),
+             _p(self.is_homo), self.homo_stop, _p(self.tok[r]), _p(self.run[r]), _p(self.pos[r]), _p(self.plen[r]),
+             _p(self.rope_off[r]), _p(self.out[r]), self.out.stride(0), self.out.shape[1], _p(self.pos32[r]),
+             _p(self.seqlens[r]), _p(self.rpos32[r]), hi - lo, w.vocab, EOS, PAD, _p(w.embed), _p(self.x[r]),
+             _p(self.ssq[r]), *noise, st)
 
     @torch.no_grad()
     def _capture(self):
