@@ -694,5 +694,171 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Persistent GEMM for large M (prefill): one CTA per SM walks the output tiles (BN = 256, N fastest, so the
+// CTAs that run together share A row blocks in L2).  Warp 0 streams A/B stages through a 4-deep TMA ring across
+// tile boundaries, warp 1 issues the MMAs into one of two TMEM accumulators (2 x 256 of the 512 columns), and
+// eight epilogue warps (two per TMEM lane quarter, each taking half of the tile's 64-column chunks) drain the
+// other accumulator, so a tile's epilogue overlaps the next tile's K loop.  Epilogues as gemm_kernel (NK = 1).
+constexpr int kPBN = 256;
+constexpr int kPStages = 4;
+constexpr int kPThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kPStageBytes = BM * BK * 2 + kPBN * BK * 2;  // 48 KB
+constexpr int kPBarOff = kPStages * kPStageBytes;
+constexpr int kPSmemBytes = kPBarOff + 256 + 1024;
+constexpr uint32_t kPTmemCols = 512;
+
+template <int EPI>
+__global__ void __launch_bounds__(kPThreads, 1)
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
+                           int N, int K, EpiArgs ep) {
+  constexpr int BN = kPBN;
+  constexpr int A_BYTES = BM * BK * 2;
+  constexpr int B_BOX_BYTES = (EPI == SWIGLU ? BN / 2 : BN) * BK * 2;
+  constexpr int W = Chunks<BN>::W;
+  constexpr int CPS = Chunks<BN>::COUNT / 2;  // chunks per epilogue warp set
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPBarOff);
+  uint64_t* empty = full + kPStages;
+  uint64_t* acc_full = empty + kPStages;   // [2] accumulator ready (tcgen05.commit)
+  uint64_t* acc_empty = acc_full + 2;      // [2] accumulator drained (8 epilogue warps)
+  uint64_t* tmem_free = acc_empty + 2;     // every epilogue warp is done with TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_free + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = (EPI == SWIGLU ? N / 2 : N) / (EPI == SWIGLU ? BN / 2 : BN);
+  const int m_tiles = (M + BM - 1) / BM;
+  const int tiles = n_tiles * m_tiles;
+  const int nkb = K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);
+    }
+    mbar_init(tmem_free, 8);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kPTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t keep = l2_policy_evict_last();
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int n_tile = t % n_tiles, m0 = (t / n_tiles) * BM;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % kPStages;
+          if (it >= kPStages && !mbar_wait(&empty[s], ((it / kPStages) & 1) ^ 1)) {
+            raise_error(ERR_WAIT_EMPTY);
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + s * kPStageBytes;
+          uint8_t* sB = sA + A_BYTES;
+          const int kx = kb * BK;
+          mbar_expect_tx(&full[s], kPStageBytes);
+          tma_load_2d(sA, &tmA, &full[s], kx, m0);
+          if (EPI == SWIGLU) {
+            tma_load_2d_hint(sB, &tmB, &full[s], kx, n_tile * (BN / 2), keep);
+            tma_load_2d_hint(sB + B_BOX_BYTES, &tmB, &full[s], kx, N / 2 + n_tile * (BN / 2), keep);
+          } else {
+            tma_load_2d_hint(sB, &tmB, &full[s], kx, n_tile * BN, keep);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      uint32_t it = 0;
+      int i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++i) {
+        const int ab = i & 1;
+        if (i >= 2 && !mbar_wait(&acc_empty[ab], ((i >> 1) - 1) & 1)) {
+          raise_error(ERR_WAIT_ACCUM);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t dacc = tmem_base + ab * BN;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % kPStages;
+          if (!mbar_wait(&full[s], (it / kPStages) & 1)) {
+            raise_error(ERR_WAIT_FULL);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sdesc_k_sw128(smem_u32(smem + s * kPStageBytes));
+          const uint64_t bd = sdesc_k_sw128(smem_u32(smem + s * kPStageBytes + A_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) umma_bf16(dacc, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[ab]);
+      }
+    }
+  } else {
+    // epilogue warps 2..9: lane quarter (warp % 4), column half (warp set)
+    const int quarter = warp & 3;
+    const int set = (warp - 2) >> 2;
+    const int row_local = quarter * 32 + lane;
+    int i = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const int ab = i & 1;
+      const int n_tile = t % n_tiles, m0 = (t / n_tiles) * BM;
+      const int row = m0 + row_local;
+      const bool row_ok = row < M;
+      const float r = (row_ok && EPI != BIAS_ACT && EPI != ADD_RESID) ? row_rscale(ep, row) : 1.f;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[ab], (i >> 1) & 1))) {
+        if (lane == 0) raise_error(ERR_WAIT_ACCUM);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ab * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+      for (int cc = 0; cc < CPS; ++cc) {
+        const int ch = set * CPS + cc;
+        float v[64];
+#pragma unroll
+        for (int q = 0; q < W; q += 16) tmem_ld16(taddr + chunk_col<BN, EPI>(ch, q), v + q);
+        tmem_wait_ld();
+        if (row_ok) epi_chunk<BN, EPI>(ep, row, n_tile, ch, v, r, N);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(tmem_free);
+  }
+  if (warp == 1) {
+    // free TMEM once the epilogue warps are done (they waited on the last accumulator, i.e. on every MMA)
+    if (!mbar_wait(tmem_free, 0) && lane == 0) raise_error(ERR_WAIT_ACCUM);
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kPTmemCols);
+  }
+}
+
 }  // namespace gemm
 }  // namespace vk

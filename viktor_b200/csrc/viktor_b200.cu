@@ -144,6 +144,35 @@ static int run_gemm(const void* A, const void* B, int64_t M, int N, int K, const
   }
 }
 
+// Large-M GEMMs (prefill): the persistent BN = 256 kernel when N fits its tiles.
+#ifndef VK_PERSISTENT_GEMM
+#define VK_PERSISTENT_GEMM 1
+#endif
+template <int EPI>
+static bool persistent_fits(int64_t M, int N) {
+  if (!VK_PERSISTENT_GEMM || M <= 0 || M > (int64_t(1) << 31) - 128) return false;
+  return EPI == gemm::SWIGLU ? (N / 2) % (gemm::kPBN / 2) == 0 && N % 2 == 0 : N % gemm::kPBN == 0;
+}
+
+template <int EPI>
+static int run_gemm_persistent(const void* A, const void* B, int64_t M, int N, int K, const gemm::EpiArgs& ep,
+                               int64_t b_rows, void* stream) {
+  if (K <= 0 || K % gemm::BK != 0) return VK_ERR_ARG;
+  if (!aligned16(A) || !aligned16(B)) return VK_ERR_ARG;
+  CUtensorMap ta, tb;
+  const uint32_t b_box = EPI == gemm::SWIGLU ? gemm::kPBN / 2 : gemm::kPBN;
+  if (!make_map_kmajor(&ta, A, static_cast<uint64_t>(M), K, K, gemm::BM)) return VK_ERR_ARG;
+  if (!make_map_kmajor(&tb, B, static_cast<uint64_t>(b_rows), K, K, b_box)) return VK_ERR_ARG;
+  const int sms = device_sm_count();
+  if (sms <= 0) return VK_ERR_CUDA;
+  const int64_t n_tiles = (EPI == gemm::SWIGLU ? N / 2 : N) / b_box;
+  const int64_t tiles = n_tiles * ((M + gemm::BM - 1) / gemm::BM);
+  auto kern = gemm::gemm_persistent_kernel<EPI>;
+  if (!ensure_smem(kern, gemm::kPSmemBytes)) return VK_ERR_CUDA;
+  return launch(kern, dim3(static_cast<unsigned>(tiles < sms ? tiles : sms)), dim3(gemm::kPThreads),
+                gemm::kPSmemBytes, stream, 1, ta, tb, static_cast<int>(M), N, K, ep);
+}
+
 static gemm::EpiArgs epi_zero() {
   gemm::EpiArgs e;
   memset(&e, 0, sizeof(e));
@@ -240,6 +269,7 @@ static int linear_impl(const void* x, const float* ssq, float eps, const void* w
       return run_gemm<128, gemm::SWIGLU>(x, w, M, N, K, ep, F / 64, N, pick_nk(M, F / 64, K), stream);
     }
     if (F % 64) return VK_ERR_ARG;
+    if (persistent_fits<gemm::SWIGLU>(M, N)) return run_gemm_persistent<gemm::SWIGLU>(x, w, M, N, K, ep, N, stream);
     return run_gemm<128, gemm::SWIGLU>(x, w, M, N, K, ep, F / 64, N, 1, stream);
   }
   ep.ldy = N;
@@ -253,6 +283,8 @@ static int linear_impl(const void* x, const float* ssq, float eps, const void* w
     const int nt = (N + 63) / 64;
     return run_gemm<64, gemm::STORE_BF16>(x, w, M, N, K, ep, nt, N, M <= kSmallM ? pick_nk(M, nt, K) : 1, stream);
   }
+  if (persistent_fits<gemm::STORE_BF16>(M, N))
+    return run_gemm_persistent<gemm::STORE_BF16>(x, w, M, N, K, ep, N, stream);
   return run_gemm<128, gemm::STORE_BF16>(x, w, M, N, K, ep, (N + 127) / 128, N, 1, stream);
 }
 
@@ -580,6 +612,8 @@ int vk_linear_qkv_rope_cache(const void* x, const float* ssq, float norm_eps, co
   const int N = (n_heads + 2 * n_kv_heads) * 64;
   if (M <= kSmallM)
     return run_gemm<64, gemm::QKV_ROPE>(x, w_qkv, M, N, 512, ep, N / 64, N, pick_nk(M, N / 64, 512), stream);
+  if (persistent_fits<gemm::QKV_ROPE>(M, N))
+    return run_gemm_persistent<gemm::QKV_ROPE>(x, w_qkv, M, N, 512, ep, N, stream);
   return run_gemm<128, gemm::QKV_ROPE>(x, w_qkv, M, N, 512, ep, N / 128, N, 1, stream);
 }
 
@@ -591,6 +625,8 @@ int vk_linear_residual(const void* a, const void* w, void* x, float* ssq_out, in
   ep.x = static_cast<__nv_bfloat16*>(x);
   ep.ssq_out = ssq_out;
   if (M <= kSmallM) return run_gemm<64, gemm::ADD_RESID>(a, w, M, 512, K, ep, 8, 512, pick_nk(M, 8, K), stream);
+  if (persistent_fits<gemm::ADD_RESID>(M, 512))
+    return run_gemm_persistent<gemm::ADD_RESID>(a, w, M, 512, K, ep, 512, stream);
   return run_gemm<128, gemm::ADD_RESID>(a, w, M, 512, K, ep, 4, 512, 1, stream);
 }
 
@@ -637,6 +673,8 @@ int vk_linear_bias_act(const void* x, const void* w, const void* bias, void* y, 
   ep.bias = static_cast<const __nv_bfloat16*>(bias);
   ep.act = act;
   if (M <= kSmallM) return run_gemm<64, gemm::BIAS_ACT>(x, w, M, N, K, ep, N / 64, N, 1, stream);
+  if (persistent_fits<gemm::BIAS_ACT>(M, N))
+    return run_gemm_persistent<gemm::BIAS_ACT>(x, w, M, N, K, ep, N, stream);
   return run_gemm<128, gemm::BIAS_ACT>(x, w, M, N, K, ep, (N + 127) / 128, N, 1, stream);
 }
 
