@@ -172,3 +172,47 @@ def test_greedy_chunks_identical_to_oracle_rate():
     print(f"identical chunks {exact:.4f} ({(got == ref).all(1).sum()} / {len(lens)})")
     assert ok.all(), np.where(~ok)[0]
     assert exact >= 0.95
+
+
+def test_sub_batches_groups_and_empty_prefix():
+    """Prefill in sub-batches of 2 (last one partial), a chunk with no frames, 1 / 2 / 3 decode groups (uneven
+    row ranges): the same tokens everywhere, and the oracle's up to each chunk's first low-margin step."""
+    from viktor_b200 import Basecaller, DecodeEngine, DecoderConfig
+    g = load("base_b8")
+    m = g["meta"]
+    lens = [5, 0, 64, 31, 200]
+    from viktor_b200.synthetic import make_frames
+    frames = make_frames(lens, seed=44)
+    model = Basecaller.from_weights(g["weights"], k=m["k"], cfg=DecoderConfig(**m["cfg"]), d_enc=m["d_enc"])
+    outs = []
+    for groups, pb in ((1, 128), (2, 2), (3, 2)):
+        eng = DecodeEngine(model, len(lens), 20, max(lens), prefill_batch=pb, max_homopolymer=None, device="cuda",
+                           decode_groups=groups)
+        eng.bias[2] = float("-inf")
+        outs.append(eng.generate(torch.from_numpy(frames), lens, 20).cpu().numpy())
+    assert all(np.array_equal(o, outs[0]) for o in outs[1:])
+    bias = np.zeros(7, np.float32)
+    bias[[0, 1, 2]] = -np.inf
+    ref, margin = oracle_for(g).generate(frames, lens, 20, steps=20, bias=bias, max_homopolymer=None)
+    ok = agree_until_low_margin(outs[0], ref, margin)
+    assert ok.all(), f"\n{outs[0]}\n{ref}"
+
+
+def test_generate_again_with_other_lengths():
+    """A second generate() with different prefix lengths (new prefill plan, longer and shorter rows) gives the
+    tokens a fresh engine gives."""
+    from viktor_b200 import Basecaller, DecodeEngine, DecoderConfig
+    from viktor_b200.synthetic import make_frames
+    g = load("base_b8")
+    m = g["meta"]
+    model = Basecaller.from_weights(g["weights"], k=m["k"], cfg=DecoderConfig(**m["cfg"]), d_enc=m["d_enc"])
+    a_lens, b_lens = [40, 7, 300], [300, 1, 120]
+    fa, fb = make_frames(a_lens, seed=45), make_frames(b_lens, seed=46)
+    eng = DecodeEngine(model, 3, 16, 300, max_homopolymer=None, device="cuda")
+    eng.bias[2] = float("-inf")
+    eng.generate(torch.from_numpy(fa), a_lens, 16)
+    got = eng.generate(torch.from_numpy(fb), b_lens, 16).cpu().numpy()
+    fresh = DecodeEngine(model, 3, 16, 300, max_homopolymer=None, device="cuda")
+    fresh.bias[2] = float("-inf")
+    ref = fresh.generate(torch.from_numpy(fb), b_lens, 16).cpu().numpy()
+    assert np.array_equal(got, ref)

@@ -141,7 +141,10 @@ class DecodeEngine:
                              device=dev)
             self._groups.append((lo, hi, ws))
         self._side_streams = [torch.cuda.Stream(dev) for _ in range(G)] if G > 1 else []
-        self._pf = None  # prefill buffers, allocated on first prefill
+        self._pf = None  # prefill scratch, allocated on first prefill and grown when a sub-batch needs more
+        # the final residual of every chunk's BOS row (and its sums of squares), kept across prefill sub-batches
+        self._xcat = torch.empty(B, cfg.d_model, dtype=_BF16, device=dev)
+        self._scat = torch.empty(B, 8, dtype=torch.float32, device=dev)
         self.graph = None
         self.kernels_per_step = 0
         if cuda_graph:
@@ -267,9 +270,7 @@ class DecodeEngine:
                       sl=torch.empty(nb, 8, dtype=torch.float32, device=dev),
                       ql=torch.empty(nb, cfg.n_heads, cfg.head_dim, dtype=_BF16, device=dev),
                       ol=torch.empty(nb, cfg.n_heads * cfg.head_dim, dtype=_BF16, device=dev),
-                      gl=torch.empty(nb, cfg.ffn_dim, dtype=_BF16, device=dev),
-                      xcat=torch.empty(self.B, cfg.d_model, dtype=_BF16, device=dev),
-                      scat=torch.empty(self.B, 8, dtype=torch.float32, device=dev))
+                      gl=torch.empty(nb, cfg.ffn_dim, dtype=_BF16, device=dev))
             self._pf = pf
         return pf
 
@@ -300,8 +301,8 @@ class DecodeEngine:
                           last_indices=plan["last"], lengths=plan["lengths"], x_last=xl, ssq_last=sl,
                           q_last=pf["ql"][:n], o_last=pf["ol"][:n], g_last=pf["gl"][:n], workspace=self.attn_ws,
                           stream=st)
-        pf["xcat"][row0:row0 + n].copy_(xl)
-        pf["scat"][row0:row0 + n].copy_(sl)
+        self._xcat[row0:row0 + n].copy_(xl)
+        self._scat[row0:row0 + n].copy_(sl)
 
     @torch.no_grad()
     def prefill(self, frames, frame_lens):
@@ -322,7 +323,7 @@ class DecodeEngine:
         for lo in range(0, self.B, self.prefill_batch):
             hi = min(self.B, lo + self.prefill_batch)
             self._prefill_sub(frames[int(offs[lo]):int(offs[hi])], frame_lens[lo:hi], lo, st)
-        xcat, scat = self._pf["xcat"][:self.B], self._pf["scat"][:self.B]
+        xcat, scat = self._xcat, self._scat
         # first token: select with prev = BOS; greedy writes column pos - plen = 0 and sets pos = plen + 1
         self.tok.fill_(BOS)
         self.run.zero_()
