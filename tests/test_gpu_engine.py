@@ -216,3 +216,21 @@ def test_generate_again_with_other_lengths():
     fresh.bias[2] = float("-inf")
     ref = fresh.generate(torch.from_numpy(fb), b_lens, 16).cpu().numpy()
     assert np.array_equal(got, ref)
+
+
+def test_pinned_host_frames_equal_device_frames():
+    """Frames in pinned host memory (copied per prefill sub-batch on a copy stream, overlapping the previous
+    sub-batch's prefill) and pageable host frames give the tokens of device-resident frames."""
+    from viktor_b200 import Basecaller, DecodeEngine, DecoderConfig
+    from viktor_b200.synthetic import make_frames
+    g = load("base_b8")
+    m = g["meta"]
+    model = Basecaller.from_weights(g["weights"], k=m["k"], cfg=DecoderConfig(**m["cfg"]), d_enc=m["d_enc"])
+    lens = [100, 37, 256, 3, 180]
+    frames = torch.from_numpy(make_frames(lens, seed=47))
+    eng = DecodeEngine(model, len(lens), 12, 256, prefill_batch=2, max_homopolymer=None, device="cuda")
+    eng.bias[2] = float("-inf")
+    ref = eng.generate(frames.cuda(), lens, 12).clone()
+    pinned = eng.generate(frames.pin_memory(), lens, 12).clone()
+    pageable = eng.generate(frames, lens, 12).clone()
+    assert torch.equal(pinned, ref) and torch.equal(pageable, ref)

@@ -141,6 +141,7 @@ class DecodeEngine:
                              device=dev)
             self._groups.append((lo, hi, ws))
         self._side_streams = [torch.cuda.Stream(dev) for _ in range(G)] if G > 1 else []
+        self._copy_stream = None  # host -> device copies of prefill frames (pinned host input)
         self._pf = None  # prefill scratch, allocated on first prefill and grown when a sub-batch needs more
         # the final residual of every chunk's BOS row (and its sums of squares), kept across prefill sub-batches
         self._xcat = torch.empty(B, cfg.d_model, dtype=_BF16, device=dev)
@@ -317,11 +318,32 @@ class DecodeEngine:
             if top >= self.cfg.max_seq_len:
                 raise ValueError("RoPE positions would exceed max_seq_len")
         st = self._stream()
-        if frames.device != self.device:
-            frames = frames.to(self.device, non_blocking=True)
         offs = np.concatenate([[0], np.cumsum(frame_lens)]).astype(np.int64)
-        for lo in range(0, self.B, self.prefill_batch):
-            hi = min(self.B, lo + self.prefill_batch)
+        subs = [(lo, min(self.B, lo + self.prefill_batch)) for lo in range(0, self.B, self.prefill_batch)]
+        ready = [None] * len(subs)
+        if frames.device != self.device:
+            if frames.is_pinned():
+                # host -> device copy per sub-batch on a copy stream, so that sub-batch i + 1 crosses PCIe while
+                # sub-batch i is prefilled
+                if self._copy_stream is None:
+                    self._copy_stream = torch.cuda.Stream(self.device)
+                cur = torch.cuda.current_stream(self.device)
+                dev_frames = torch.empty(frames.shape, dtype=frames.dtype, device=self.device)
+                cs = self._copy_stream
+                cs.wait_stream(cur)
+                for i, (lo, hi) in enumerate(subs):
+                    a, b = int(offs[lo]), int(offs[hi])
+                    with torch.cuda.stream(cs):
+                        dev_frames[a:b].copy_(frames[a:b], non_blocking=True)
+                        ready[i] = torch.cuda.Event()
+                        ready[i].record(cs)
+                dev_frames.record_stream(cs)
+                frames = dev_frames
+            else:
+                frames = frames.to(self.device)
+        for i, (lo, hi) in enumerate(subs):
+            if ready[i] is not None:
+                torch.cuda.current_stream(self.device).wait_event(ready[i])
             self._prefill_sub(frames[int(offs[lo]):int(offs[hi])], frame_lens[lo:hi], lo, st)
         xcat, scat = self._xcat, self._scat
         # first token: select with prev = BOS; greedy writes column pos - plen = 0 and sets pos = plen + 1
