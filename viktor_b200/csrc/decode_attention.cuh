@@ -270,18 +270,29 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (!*last_flag) return;
   __threadfence();
   const int64_t base = static_cast<int64_t>(b) * a.max_splits * 8 + hh;
-  float Mt = -INFINITY;
-  for (int sp = 0; sp < nsplit; ++sp) Mt = fmaxf(Mt, __ldcg(a.ws_ml + (base + sp * 8) * 2));
-  float Lt = 0.f, Ot[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int sp = 0; sp < nsplit; ++sp) {
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.ws_ml + (base + sp * 8) * 2));
-    const float f = exp2f(ml.x - Mt);
-    Lt += f * ml.y;
-    const float4 ov = __ldcg(reinterpret_cast<const float4*>(a.ws_o + (base + sp * 8) * 64 + d0));
-    Ot[0] += f * ov.x;
-    Ot[1] += f * ov.y;
-    Ot[2] += f * ov.z;
-    Ot[3] += f * ov.w;
+  // one pass over the splits, four at a time (their loads in flight together), merged with a running maximum
+  float Mt = -INFINITY, Lt = 0.f, Ot[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int sp0 = 0; sp0 < nsplit; sp0 += 4) {
+    float2 ml[4];
+    float4 ov[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int sp = sp0 + k < nsplit ? sp0 + k : sp0;
+      ml[k] = __ldcg(reinterpret_cast<const float2*>(a.ws_ml + (base + sp * 8) * 2));
+      ov[k] = __ldcg(reinterpret_cast<const float4*>(a.ws_o + (base + sp * 8) * 64 + d0));
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (sp0 + k >= nsplit) break;
+      const float Mn = fmaxf(Mt, ml[k].x);
+      const float fa = exp2f(Mt - Mn), fb = exp2f(ml[k].x - Mn);
+      Lt = Lt * fa + ml[k].y * fb;
+      Ot[0] = Ot[0] * fa + ov[k].x * fb;
+      Ot[1] = Ot[1] * fa + ov[k].y * fb;
+      Ot[2] = Ot[2] * fa + ov[k].z * fb;
+      Ot[3] = Ot[3] * fa + ov[k].w * fb;
+      Mt = Mn;
+    }
   }
   const float inv = 1.f / Lt;
   *reinterpret_cast<uint2*>(op) = make_uint2(pack_bf16x2(Ot[0] * inv, Ot[1] * inv), pack_bf16x2(Ot[2] * inv, Ot[3] * inv));
