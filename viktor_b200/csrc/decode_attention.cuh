@@ -70,6 +70,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   pdl_launch_dependents();
+  if (threadIdx.x == 128 && b < a.nq) {
+    // While the previous kernel finishes: the first tiles of this split into L2.  Cache rows older than this
+    // step's newest position were written by earlier grids; the prefetch only warms L2 (the loads after the
+    // wait read whatever L2 then holds).
+    const int p0 = split * a.chunk, crow = a.row0 + b;
+    for (int t = 0; t < kStages; ++t)
+      for (int h = 0; h < 2; ++h) {
+        tma_prefetch_l2_4d(&tmK, 0, h, p0 + t * kTile, crow);
+        tma_prefetch_l2_4d(&tmV, 0, h, p0 + t * kTile, crow);
+      }
+  }
   pdl_wait();  // q, lengths and the newest cache row come from the previous kernel
   if (b >= a.nq) return;
   const int L = a.lengths[b];

@@ -150,6 +150,13 @@ VK_DEV void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
                : "memory");
 }
 
+VK_DEV void tma_prefetch_l2_4d(const CUtensorMap* map, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+
 // ---- programmatic dependent launch ---------------------------------------------------------------------------
 VK_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 VK_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
