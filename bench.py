@@ -196,6 +196,42 @@ def attention_roofline(eng, torch, lens, steps):
     return nbytes, t
 
 
+def attention_roofline_i8(eng, torch, lens, steps):
+    """The same measurement for the opt-in int8-prefix kernel (vk_decode_attention_i8): algorithmic bytes =
+    int8 prefix (256 B per position) + bf16 tail (512 B per position) + per-channel scales + q read + o written."""
+    from viktor_b200._lib import call
+    B = eng.B
+    mid = torch.tensor([n + 1 + steps // 2 for n in lens], dtype=torch.int32, device=eng.device)
+    st = torch.cuda.current_stream(eng.device)
+    reps = 5
+    kc, vc = eng.cache.k, eng.cache.v
+    from viktor_b200._lib import load
+    ws = torch.zeros(load().vk_decode_attention_i8_workspace_bytes(B, eng.prefix8[0].S8, eng.max_tail),
+                     dtype=torch.uint8, device=eng.device)
+
+    def launch(i):
+        pre = eng.prefix8[i]
+        call("vk_decode_attention_i8", eng.q.data_ptr(), kc[i].data_ptr(), vc[i].data_ptr(), pre.k8.data_ptr(),
+             pre.v8t.data_ptr(), pre.sk.data_ptr(), pre.sv.data_ptr(), eng.starts.data_ptr(), mid.data_ptr(),
+             eng.o.data_ptr(), B, 0, kc.shape[1], kc.shape[2], kc[i].stride(0), kc[i].stride(1), pre.S8,
+             eng.max_tail, ws.data_ptr(), ws.numel(), st.cuda_stream)
+
+    for i in range(8):
+        launch(i)
+    torch.cuda.synchronize(eng.device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        for i in range(8):
+            launch(i)
+    e1.record(st)
+    torch.cuda.synchronize(eng.device)
+    t = e0.elapsed_time(e1) / 1e3 / (reps * 8)
+    starts = eng.starts.long()
+    nbytes = int(starts.sum().item()) * 256 + int((mid.long() - starts).sum().item()) * 512 + B * (1024 * 2 + 1024)
+    return nbytes, t
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -209,6 +245,8 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=None, help="CPU-baseline decode steps (default: workload's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--kv-int8", action="store_true",
+                    help="opt-in int8 prefix KV (own tolerance; the headline number is the bf16 path)")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.decode_steps:
@@ -241,7 +279,8 @@ def main():
     dcfg = DecoderConfig(vocab_size=V, rope_theta=1e6)
     model = Basecaller.from_weights(make_weights(dcfg, seed=0, init="normal"), k=cfg["k"], cfg=dcfg)
     lens = make_lens(cfg, B, seed=100 + rank)
-    eng = DecodeEngine(model, B, steps, PLEN, max_homopolymer=None, device=dev, decode_groups=args.decode_groups)
+    eng = DecodeEngine(model, B, steps, PLEN, max_homopolymer=None, device=dev, decode_groups=args.decode_groups,
+                       kv_int8=args.kv_int8)
     eng.bias[2] = float("-inf")  # EOS masked: fixed-length decode, every step emits a base
     n_bases = torch.as_tensor(model.tokenizer.n_bases, device=dev)
     g = torch.Generator(device=dev)
@@ -323,6 +362,12 @@ def main():
                 if peak_kind == "measured" else "fallback 6.65 TB/s",
                 "bytes_per_launch": nbytes, "launch_us": t_attn * 1e6,
                 "traffic": None if ratio is None else nbytes * ratio}
+    roofline_i8 = None
+    if args.kv_int8:
+        nb8, t8 = attention_roofline_i8(eng, torch, lens, steps)
+        roofline_i8 = {"bound": "hbm", "kernel": "decode_attn_i8_kernel", "achieved": nb8 / t8 / 1e9, "peak": peak,
+                       "unit": "GB/s", "frac": nb8 / t8 / 1e9 / peak, "bytes_per_launch": nb8,
+                       "launch_us": t8 * 1e6}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args, cfg)
@@ -338,6 +383,9 @@ def main():
                 "prefill_ms_per_chunk": prefill_s / (args.steps * B) * 1e3,
                 "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "clocks": clk.summary()}
+        if args.kv_int8:
+            line["config"]["kv_int8"] = "prefix K/V int8 with per-channel scales, generated tokens bf16"
+            line["roofline_int8"] = roofline_i8
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

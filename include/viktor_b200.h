@@ -112,6 +112,31 @@ int vk_decode_attention(const void* q, const void* k_cache, const void* v_cache,
                         void* out, int nq, int row0, int cache_rows, int S, int64_t stride_kb, int64_t stride_ks,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- opt-in INT8 prefix KV (the reference's analysis.md:95 proposal; no reference kernel exists) ------------
+ * The prefix of a chunk (its prefilled positions) is written once; an int8 copy halves the bytes decode
+ * attention reads for it, while generated tokens stay bf16.  Per channel c of one layer and row (both KV heads,
+ * 128 channels): s_c = max_{p < start} |x[p][c]| / 127, stored byte u = clamp(rint(x / s_c), -127, 127) + 128.
+ * k8 [cache_rows][S8][128] u8 (position-major), v8t [cache_rows][128][S8] u8 (channel-major), sk/sv
+ * [cache_rows][128] f32; S8 a multiple of 128. */
+
+/* Quantizes positions [0, starts[i]) (0 <= starts[i] <= min(S, S8), i32) of cache row row0 + i, i < n, of one
+ * layer (same cache layout as vk_decode_attention) into k8/v8t/sk/sv. */
+int vk_kv_quantize(const void* k_cache, const void* v_cache, int cache_rows, int S, int64_t stride_kb,
+                   int64_t stride_ks, const int32_t* starts, int row0, int n, void* k8, void* v8t, float* sk,
+                   float* sv, int S8, void* stream);
+
+/* Workspace bytes vk_decode_attention_i8 needs (zero-filled once before first use, like vk_decode_attention's). */
+size_t vk_decode_attention_i8_workspace_bytes(int nq, int S8, int max_tail);
+
+/* vk_decode_attention with positions [0, starts[i]) of query i read from the int8 copy (vk_kv_quantize) and
+ * [starts[i], lengths[i]) from the bf16 cache.  Requires 0 <= starts[i] < lengths[i] <= S, starts[i] <= S8 and
+ * lengths[i] - starts[i] <= max_tail (violations set the device error flag and skip the query). */
+int vk_decode_attention_i8(const void* q, const void* k_cache, const void* v_cache, const void* k8,
+                           const void* v8t, const float* sk, const float* sv, const int32_t* starts,
+                           const int32_t* lengths, void* out, int nq, int row0, int cache_rows, int S,
+                           int64_t stride_kb, int64_t stride_ks, int S8, int max_tail, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* Decode attention for callers that cannot allocate device memory.  No counterpart in the reference: it is
  * vk_decode_attention with its split-K workspace taken from a fixed array inside this library instead of from
  * the caller.  Meant for hosts that hand a kernel only its inputs and outputs and have no way to obtain a
@@ -217,6 +242,26 @@ int vk_prefill_plan(const int32_t* lens, int n, int row0, int pos_scale, int64_t
 /* x[rows[i], :] = emb[token, :] (d bf16 values per row). */
 int vk_scatter_embed(void* x, const int64_t* rows, int64_t n, int64_t x_rows, const void* emb, int64_t token,
                      int d, void* stream);
+
+
+/* ---- host-side stitching of chunk calls (scripts/basecall_viktor.py:31-108; no device work) -----------------
+ * Edit-distance alignment with edlib's semantics (the reference's aligner): mode 0 NW (global), 1 SHW (query
+ * against a prefix of the target), 2 HW (query against an infix); k >= 0 caps the distance (above it: -1).
+ * out[3] = distance, start and end (inclusive, -1: no target base) of the first best location; with
+ * cigar != NULL (cigar_cap >= qlen + tlen + 1) the alignment path as extended CIGAR operations, one character
+ * per column ('=', 'X', 'I' = query base not in the target, 'D' = target base not in the query), NUL-ended. */
+int vk_align(const char* query, int qlen, const char* target, int tlen, int mode, int k, int* out, char* cigar,
+             int cigar_cap);
+
+/* scripts/basecall_viktor.py:31-54 overlap_cut: calls a, b of adjacent chunks sharing ov_frames encoder frames,
+ * rate = bases per frame of a; keep a[:cut[0]] + b[cut[1]:]. */
+int vk_overlap_cut(const char* a, int la, const char* b, int lb, int ov_frames, double rate, int* cut);
+
+/* scripts/basecall_viktor.py:96-108 stitch: the n calls of one read, concatenated (call i is
+ * calls[offsets[i], offsets[i + 1])), spans [n][2] their (start, end) samples, stride samples per encoder frame.
+ * Writes the read's sequence to out (cap bytes) and its length to out_len; out == NULL only reports the length. */
+int vk_stitch(const char* calls, const int64_t* offsets, const int64_t* spans, int n, int stride, char* out,
+              int64_t cap, int64_t* out_len);
 
 #ifdef __cplusplus
 }

@@ -62,3 +62,26 @@ def test_torch_cpu_baseline_port_matches_reference(name):
     tm = TorchCPUModel(OracleConfig(**m["cfg"]), g["weights"], k=m["k"])
     out = tm.generate(g["frames"], m["lens"], m["max_new"], g["bias"], m["max_homopolymer"])
     np.testing.assert_array_equal(out, g["tokens"])
+
+
+def test_kv_int8_oracle_known_answers():
+    """The int8 prefix rule on hand-computed columns: s = max|x| / 127, byte = rint(x * 127 / max) + 128 (half to
+    even), an all-zero channel has scale 0 and bytes 128; dequantized attention over an exactly representable
+    prefix equals the bf16 attention."""
+    from oracle.kv_int8_np import decode_attention, decode_attention_i8, quantize_prefix
+    x = np.zeros((3, 128), np.float32)
+    x[:, 0] = [-1.0, 0.5, 1.0]
+    x[:, 2] = [2.0, -0.01, 0.0]
+    u, s = quantize_prefix(x)
+    assert u[:, 0].tolist() == [1, 192, 255]
+    assert u[:, 1].tolist() == [128, 128, 128] and s[1] == 0
+    assert u[:, 2].tolist() == [255, 127, 128]
+    assert s[0] == np.float32(1) / np.float32(127) and s[2] == np.float32(2) / np.float32(127)
+    rng = np.random.default_rng(0)
+    k = rng.integers(-127, 128, (40, 2, 64)).astype(np.float32)
+    k[0] = 127.0  # every channel's maximum is 127: the prefix quantizes without error
+    v = rng.integers(-127, 128, (40, 2, 64)).astype(np.float32)
+    v[0] = -127.0
+    q = rng.standard_normal((8, 64)).astype(np.float32) * 0.05
+    got, *_ = decode_attention_i8(q, k, v, 30)
+    assert np.allclose(got, decode_attention(q, k, v), atol=1e-9)

@@ -36,6 +36,13 @@ _SIGS = {
                                p, p, i64, f32, p]),
     "vk_decode_attention_workspace_bytes": (sz, [i32, i32]),
     "vk_decode_attention": (i32, [p, p, p, p, p, i32, i32, i32, i32, i64, i64, p, sz, p]),
+    "vk_kv_quantize": (i32, [p, p, i32, i32, i64, i64, p, i32, i32, p, p, p, p, i32, p]),
+    "vk_decode_attention_i8_workspace_bytes": (sz, [i32, i32, i32]),
+    "vk_decode_attention_i8": (i32, [p, p, p, p, p, p, p, p, p, p, i32, i32, i32, i32, i64, i64, i32, i32, p, sz,
+                                     p]),
+    "vk_align": (i32, [p, i32, p, i32, i32, i32, p, p, i32]),
+    "vk_overlap_cut": (i32, [p, i32, p, i32, i32, C.c_double, p]),
+    "vk_stitch": (i32, [p, p, p, i32, i32, p, i64, p]),
     "vk_decode_attention_noalloc": (i32, [p, p, p, p, p, i32, i32, i32, i32, i64, i64, p]),
     "vk_prefill_attention": (i32, [p, p, p, p, i32, i32, i64, i32, i32, i32, i64, i64, p, p]),
     "vk_linear_rmsnorm": (i32, [p, p, f32, p, p, i64, i32, i32, i32, i32, p]),
@@ -54,7 +61,8 @@ _SIGS = {
 }
 
 _lib = None
-_HOST_ONLY = {"vk_version", "vk_read_device_errors", "vk_set_pdl", "vk_decode_attention_workspace_bytes"}
+_HOST_ONLY = {"vk_version", "vk_read_device_errors", "vk_set_pdl", "vk_decode_attention_workspace_bytes",
+              "vk_decode_attention_i8_workspace_bytes", "vk_align", "vk_overlap_cut", "vk_stitch"}
 launches = 0  # kernels launched through call() (each launching entry point launches exactly one kernel)
 
 

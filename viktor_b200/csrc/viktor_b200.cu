@@ -8,6 +8,7 @@
 #include "elementwise.cuh"
 #include "gemm_tc.cuh"
 #include "prefill_attention.cuh"
+#include "stitch_host.h"
 #include "vk_host.cuh"
 
 namespace vk {
@@ -473,6 +474,7 @@ int vk_decode_attention(const void* q, const void* k_cache, const void* v_cache,
   int chunk = 1024;
   while (chunk > attn::kMinChunk && static_cast<int64_t>(nq) * ((S + chunk - 1) / chunk) < 2 * sms) chunk /= 2;
   attn::DecodeArgs a;
+  memset(&a, 0, sizeof(a));
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.out = static_cast<__nv_bfloat16*>(out);
   a.lengths = lengths;
@@ -490,6 +492,117 @@ int vk_decode_attention(const void* q, const void* k_cache, const void* v_cache,
   if (!ensure_smem(attn::decode_attn_kernel, attn::kSmemBytes)) return VK_ERR_CUDA;
   return launch(attn::decode_attn_kernel, dim3((S + chunk - 1) / chunk, nq), dim3(attn::kThreads), attn::kSmemBytes,
                 stream, 1, mk, mv, a);
+}
+
+// ---- int8 prefix KV ------------------------------------------------------------------------------------------
+// Split plan of decode_attn_i8_kernel: bf16 splits of `chunk` positions and at most n8max int8 splits of about
+// 2 x chunk positions (the same bytes per CTA), the longest chunk that still fills every SM twice.
+struct I8Plan {
+  int chunk, n8max, n16max;
+};
+static I8Plan i8_plan(int nq, int S8, int max_tail, int sms) {
+  I8Plan p{};
+  for (int c = 1024;; c /= 2) {
+    p.chunk = c;
+    p.n8max = (S8 + 2 * c - 1) / (2 * c);
+    p.n16max = (max_tail + c - 1) / c;
+    if (c == 128 || static_cast<int64_t>(nq) * (p.n8max + p.n16max) >= 2 * sms) break;
+  }
+  return p;
+}
+static size_t i8_slots_bound(int S8, int max_tail) { return (S8 + 255) / 256 + (max_tail + 127) / 128; }
+
+size_t vk_decode_attention_i8_workspace_bytes(int nq, int S8, int max_tail) {
+  if (nq <= 0 || S8 <= 0 || max_tail <= 0) return 0;
+  const size_t splits = i8_slots_bound(S8, max_tail);
+  const size_t counters = ((size_t)nq * 4 + 255) / 256 * 256;
+  const size_t ml = ((size_t)nq * splits * 8 * 2 * 4 + 255) / 256 * 256;
+  return counters + ml + (size_t)nq * splits * 8 * 64 * 4;
+}
+
+int vk_kv_quantize(const void* k_cache, const void* v_cache, int cache_rows, int S, int64_t stride_kb,
+                   int64_t stride_ks, const int32_t* starts, int row0, int n, void* k8, void* v8t, float* sk,
+                   float* sv, int S8, void* stream) {
+  if (n == 0) return VK_OK;
+  if (n < 0 || !k_cache || !v_cache || !starts || !k8 || !v8t || !sk || !sv || S <= 0 || row0 < 0 ||
+      row0 + n > cache_rows || S8 <= 0 || S8 % 128 != 0 || stride_ks < 128 || stride_ks % 8 != 0 ||
+      stride_kb < stride_ks * S || stride_kb % 8 != 0)
+    return VK_ERR_ARG;
+  if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(k8) || !aligned16(v8t) || !aligned16(sk) ||
+      !aligned16(sv))
+    return VK_ERR_ARG;
+  attn::QuantArgs a;
+  a.k = static_cast<const __nv_bfloat16*>(k_cache);
+  a.v = static_cast<const __nv_bfloat16*>(v_cache);
+  a.stride_kb = stride_kb;
+  a.stride_ks = stride_ks;
+  a.starts = starts;
+  a.row0 = row0;
+  a.n = n;
+  a.S = S;
+  a.S8 = S8;
+  a.k8 = static_cast<uint8_t*>(k8);
+  a.v8t = static_cast<uint8_t*>(v8t);
+  a.sk = sk;
+  a.sv = sv;
+  return launch(attn::kv_quantize_kernel, dim3(n, 2), dim3(attn::kQuantThreads), 0, stream, 1, a);
+}
+
+int vk_decode_attention_i8(const void* q, const void* k_cache, const void* v_cache, const void* k8,
+                           const void* v8t, const float* sk, const float* sv, const int32_t* starts,
+                           const int32_t* lengths, void* out, int nq, int row0, int cache_rows, int S,
+                           int64_t stride_kb, int64_t stride_ks, int S8, int max_tail, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (nq == 0) return VK_OK;
+  if (nq < 0 || !q || !k_cache || !v_cache || !k8 || !v8t || !sk || !sv || !starts || !lengths || !out ||
+      !workspace || S <= 0 || row0 < 0 || row0 + nq > cache_rows || stride_ks < 128 || stride_kb < stride_ks * S ||
+      S8 <= 0 || S8 % 128 != 0 || max_tail <= 0 || max_tail > S)
+    return VK_ERR_ARG;
+  if (!aligned16(q) || !aligned16(out) || !aligned16(workspace) || !aligned16(sk) || !aligned16(sv))
+    return VK_ERR_ARG;
+  if (workspace_bytes < vk_decode_attention_i8_workspace_bytes(nq, S8, max_tail)) return VK_ERR_ARG;
+  CUtensorMap mk, mv, mk8, mv8;
+  if (!make_cache_maps(&mk, &mv, k_cache, v_cache, cache_rows, S, stride_kb, stride_ks)) return VK_ERR_ARG;
+  {
+    uint64_t dims[3] = {128, static_cast<uint64_t>(S8), static_cast<uint64_t>(cache_rows)};
+    uint64_t strides[2] = {128, static_cast<uint64_t>(S8) * 128};
+    uint32_t box[3] = {128, attn::kTile8, 1};
+    if (!make_map_u8(&mk8, k8, 3, dims, strides, box, true)) return VK_ERR_ARG;
+  }
+  {
+    uint64_t dims[3] = {static_cast<uint64_t>(S8), 128, static_cast<uint64_t>(cache_rows)};
+    uint64_t strides[2] = {static_cast<uint64_t>(S8), static_cast<uint64_t>(S8) * 128};
+    uint32_t box[3] = {attn::kTile8, 128, 1};
+    if (!make_map_u8(&mv8, v8t, 3, dims, strides, box, true)) return VK_ERR_ARG;
+  }
+  const int sms = device_sm_count();
+  if (sms <= 0) return VK_ERR_CUDA;
+  const I8Plan plan = i8_plan(nq, S8, max_tail, sms);
+  attn::DecodeArgs a;
+  memset(&a, 0, sizeof(a));
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.lengths = lengths;
+  a.row0 = row0;
+  a.nq = nq;
+  a.max_splits = plan.n8max + plan.n16max;
+  a.S = S;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  a.counters = reinterpret_cast<int*>(ws);
+  const size_t counters = ((size_t)nq * 4 + 255) / 256 * 256;
+  a.ws_ml = reinterpret_cast<float*>(ws + counters);
+  a.ws_o = reinterpret_cast<float*>(ws + counters + ((size_t)nq * a.max_splits * 8 * 2 * 4 + 255) / 256 * 256);
+  a.scale_log2 = 0.125f * 1.4426950408889634f;
+  a.chunk = plan.chunk;
+  a.starts = starts;
+  a.n8max = plan.n8max;
+  a.max_tail = max_tail;
+  a.sk = sk;
+  a.sv = sv;
+  a.S8 = S8;
+  if (!ensure_smem(attn::decode_attn_i8_kernel, attn::kSmemBytes)) return VK_ERR_CUDA;
+  return launch(attn::decode_attn_i8_kernel, dim3(plan.n8max + plan.n16max, nq), dim3(attn::kThreads),
+                attn::kSmemBytes, stream, 1, mk, mv, mk8, mv8, a);
 }
 
 }  // extern "C"
@@ -711,6 +824,61 @@ int vk_scatter_embed(void* x, const int64_t* rows, int64_t n, int64_t x_rows, co
     return VK_ERR_ARG;
   return launch(ew::scatter_embed_kernel, dim3(static_cast<unsigned>(n)), dim3(64), 0, stream, 1,
                 static_cast<__nv_bfloat16*>(x), rows, n, x_rows, static_cast<const __nv_bfloat16*>(emb), token, d);
+}
+
+// ---- host-side stitching (no device work) ------------------------------------------------------------------
+int vk_align(const char* query, int qlen, const char* target, int tlen, int mode, int k, int* out, char* cigar,
+             int cigar_cap) {
+  if (qlen < 0 || tlen < 0 || (qlen && !query) || (tlen && !target) || !out || mode < 0 || mode > 2)
+    return VK_ERR_ARG;
+  if (cigar && cigar_cap < qlen + tlen + 1) return VK_ERR_ARG;
+  const vk::stitch::Alignment r = vk::stitch::align(query, qlen, target, tlen, mode, k, cigar != nullptr);
+  out[0] = r.dist;
+  out[1] = r.start;
+  out[2] = r.end;
+  if (cigar) {
+    const size_t n = r.dist < 0 ? 0 : r.ops.size();
+    memcpy(cigar, r.ops.data(), n);
+    cigar[n] = 0;
+  }
+  return VK_OK;
+}
+
+int vk_overlap_cut(const char* a, int la, const char* b, int lb, int ov_frames, double rate, int* cut) {
+  if (la < 0 || lb < 0 || (la && !a) || (lb && !b) || !cut) return VK_ERR_ARG;
+  const vk::stitch::Cut c = vk::stitch::overlap_cut(std::string(a, a + la), std::string(b, b + lb), ov_frames, rate);
+  cut[0] = c.a;
+  cut[1] = c.b;
+  return VK_OK;
+}
+
+int vk_stitch(const char* calls, const int64_t* offsets, const int64_t* spans, int n, int stride, char* out,
+              int64_t cap, int64_t* out_len) {
+  if (n < 0 || stride <= 0 || !out_len || (n && (!calls || !offsets || !spans))) return VK_ERR_ARG;
+  std::vector<std::string> cs(n);
+  for (int i = 0; i < n; ++i) {
+    if (offsets[i + 1] < offsets[i]) return VK_ERR_ARG;
+    cs[i].assign(calls + offsets[i], calls + offsets[i + 1]);
+  }
+  std::string res;
+  int64_t cut_prev = 0;
+  for (int i = 0; i < n; ++i) {
+    const std::string& s = cs[i];
+    if (i + 1 < n) {
+      const int64_t ov = vk::stitch::floor_div(spans[2 * i + 1] - spans[2 * (i + 1)], stride);
+      const int64_t frames = std::max<int64_t>(vk::stitch::floor_div(spans[2 * i + 1] - spans[2 * i], stride), 1);
+      const double rate = static_cast<double>(s.size()) / static_cast<double>(frames);
+      const vk::stitch::Cut c = vk::stitch::overlap_cut(s, cs[i + 1], static_cast<int>(ov), rate);
+      res += vk::stitch::py_slice(s, cut_prev, c.a);
+      cut_prev = c.b;
+    } else {
+      res += vk::stitch::py_slice(s, cut_prev, static_cast<int64_t>(s.size()));
+    }
+  }
+  *out_len = static_cast<int64_t>(res.size());
+  if (!out || cap < static_cast<int64_t>(res.size())) return out ? VK_ERR_ARG : VK_OK;
+  memcpy(out, res.data(), res.size());
+  return VK_OK;
 }
 
 }  // extern "C"

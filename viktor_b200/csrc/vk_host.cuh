@@ -28,9 +28,10 @@ inline EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Tensor map over a bf16 tensor. dims/strides innermost first; strides in bytes for dims 1.. (rank-1 values).
-inline bool make_map_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                          const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128) {
+// Tensor map over a bf16 (or uint8) tensor. dims/strides innermost first; strides in bytes for dims 1.. (rank-1
+// values).
+inline bool make_map(CUtensorMap* map, CUtensorMapDataType type, const void* base, int rank, const uint64_t* dims,
+                     const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128) {
   EncodeTiledFn fn = encode_fn();
   if (!fn || !base) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
@@ -45,11 +46,18 @@ inline bool make_map_bf16(CUtensorMap* map, const void* base, int rank, const ui
       s[i] = strides_bytes[i];
     }
   }
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s, b, e,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+  CUresult r = fn(map, type, rank, const_cast<void*>(base), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+inline bool make_map_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                          const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128) {
+  return make_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, rank, dims, strides_bytes, box, swizzle128);
+}
+inline bool make_map_u8(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                        const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128) {
+  return make_map(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, rank, dims, strides_bytes, box, swizzle128);
 }
 
 // Row-major [rows, cols] bf16 matrix, K-major operand box [box_rows, 64] with 128-byte swizzle.

@@ -27,6 +27,7 @@ from ._lib import call, check_device_errors, load
 from .config import BOS, EOS, PAD
 from .decoder import KVCache
 from .fast_decoder import DeviceWeights, FastDecoder
+from .ops import PrefixKV8
 
 _BF16 = torch.bfloat16
 
@@ -70,7 +71,7 @@ class DecodeEngine:
     def __init__(self, model, batch_size: int, max_new_tokens: int, max_frames: int, backend: str = "auto",
                  cuda_graph: bool = True, prefill_batch: int = 128, check_every: int = 32,
                  attention_backend: str = "auto", temperature: float = 0.0, max_homopolymer: int | None = 64,
-                 device=None, decode_groups: int = 2):
+                 device=None, decode_groups: int = 2, kv_int8: bool = False):
         if backend not in ("auto", "cuda", "triton"):
             raise ValueError(f"backend {backend!r}: this engine runs the B200 CUDA kernels only")
         if attention_backend not in ("auto", "cuda", "triton", "flash"):
@@ -146,6 +147,17 @@ class DecodeEngine:
         # the final residual of every chunk's BOS row (and its sums of squares), kept across prefill sub-batches
         self._xcat = torch.empty(B, cfg.d_model, dtype=_BF16, device=dev)
         self._scat = torch.empty(B, 8, dtype=torch.float32, device=dev)
+        # Opt-in INT8 prefix KV (the reference's analysis.md:95 proposal): after prefill, every layer's prefix
+        # (frames + BOS) is copied into int8 with per-channel scales and decode attention reads that copy, while the
+        # generated tokens' K/V stay bf16.  Changes the arithmetic: a mode with its own tolerance, off by default.
+        self.kv_int8 = bool(kv_int8)
+        if self.kv_int8:
+            self.prefix8 = [PrefixKV8(B, max_frames + 1, dev) for _ in range(cfg.n_layers)]
+            self.starts = torch.zeros(B, dtype=torch.int32, device=dev)
+            self.max_tail = max_new_tokens + 1
+            S8 = self.prefix8[0].S8
+            self._ws8 = [torch.zeros(load().vk_decode_attention_i8_workspace_bytes(hi - lo, S8, self.max_tail),
+                                     dtype=torch.uint8, device=dev) for lo, hi, _ in self._groups]
         self.graph = None
         self.kernels_per_step = 0
         if cuda_graph:
@@ -165,23 +177,27 @@ class DecodeEngine:
         if self.noise is not None:
             self._draw_noise()
         if not self._side_streams:
-            lo, hi, ws = self._groups[0]
-            self._step_rows(lo, hi, ws, self._stream())
+            self._step_rows(0, self._stream())
             return
         main = torch.cuda.current_stream(self.device)
-        for (lo, hi, ws), side in zip(self._groups, self._side_streams):
+        for gi, side in enumerate(self._side_streams):
             side.wait_stream(main)
             with torch.cuda.stream(side):
-                self._step_rows(lo, hi, ws, side.cuda_stream)
+                self._step_rows(gi, side.cuda_stream)
         for side in self._side_streams:
             main.wait_stream(side)
 
-    def _step_rows(self, lo, hi, ws, st):
-        """One decode step of the sequences in rows [lo, hi)."""
+    def _step_rows(self, gi, st):
+        """One decode step of the sequences in the rows [lo, hi) of decode group gi."""
+        lo, hi, ws = self._groups[gi]
         r = slice(lo, hi)
         rp = None if self.pos_scale == 1 else self.rpos32[r]
+        prefix = None
+        if self.kv_int8:
+            ws = self._ws8[gi]
+            prefix = dict(layers=self.prefix8, starts=self.starts[r], max_tail=self.max_tail)
         self.fast.decode(self.x[r], self.ssq[r], self.pos32[r], self.rows[r], self.seqlens[r], self.cache, self.q[r],
-                         self.o[r], self.g[r], ws, rope_pos=rp, stream=st, row0=lo)
+                         self.o[r], self.g[r], ws, rope_pos=rp, stream=st, row0=lo, prefix=prefix)
         self._head_select(self.x[r], self.ssq[r], st, lo, hi)
 
     def _head_select(self, x, ssq, st, lo=0, hi=None):
@@ -304,6 +320,13 @@ class DecodeEngine:
                           stream=st)
         self._xcat[row0:row0 + n].copy_(xl)
         self._scat[row0:row0 + n].copy_(sl)
+        if self.kv_int8:
+            starts = plan["lengths"]  # prefix positions of each chunk: its frames and BOS
+            kc, vc = self.cache.k, self.cache.v
+            for i, pre in enumerate(self.prefix8):
+                call("vk_kv_quantize", _p(kc[i]), _p(vc[i]), kc.shape[1], kc.shape[2], kc.stride(1), kc.stride(2),
+                     _p(starts), row0, n, _p(pre.k8), _p(pre.v8t), _p(pre.sk), _p(pre.sv), pre.S8, st)
+            self.starts[row0:row0 + n].copy_(starts)
 
     @torch.no_grad()
     def prefill(self, frames, frame_lens):

@@ -137,14 +137,26 @@ class FastDecoder:
             self._mlp_tail(i, o, x, ssq, g, stream)
 
     # -- one decode step -----------------------------------------------------------------------------------------
-    def decode(self, x, ssq, pos32, rows, seqlens, cache, q, o, g, workspace, rope_pos=None, stream=None, row0=0):
+    def _decode_attn_i8(self, i, q, lengths, cache, prefix, out, workspace, row0, stream):
+        kc, vc = cache.k[i], cache.v[i]
+        pre = prefix["layers"][i]
+        call("vk_decode_attention_i8", _p(q), _p(kc), _p(vc), _p(pre.k8), _p(pre.v8t), _p(pre.sk), _p(pre.sv),
+             _p(prefix["starts"]), _p(lengths), _p(out), q.shape[0], row0, kc.shape[0], kc.shape[1], kc.stride(0),
+             kc.stride(1), pre.S8, prefix["max_tail"], _p(workspace), workspace.numel(), stream)
+
+    def decode(self, x, ssq, pos32, rows, seqlens, cache, q, o, g, workspace, rope_pos=None, stream=None, row0=0,
+               prefix=None):
         """One token per sequence: x [B, d] residual and ssq [B, 8] (from the previous step's greedy kernel);
         pos32/rows [B] int32 (rows = cache row of each sequence, row0 + arange(B)); seqlens = pos + 1.  Leaves
-        the final residual in x (and its ssq)."""
+        the final residual in x (and its ssq).  prefix (int8 prefix KV): dict(layers=[PrefixKV8 per layer],
+        starts=[B] int32, max_tail=int); workspace is then vk_decode_attention_i8's."""
         stream = torch.cuda.current_stream(x.device).cuda_stream if stream is None else stream
         for i in range(self.cfg.n_layers):
             self._qkv(i, x, ssq, pos32, rows, rope_pos, cache, q, stream)
-            self._decode_attn(i, q, seqlens, cache, o, workspace, row0, stream)
+            if prefix is None:
+                self._decode_attn(i, q, seqlens, cache, o, workspace, row0, stream)
+            else:
+                self._decode_attn_i8(i, q, seqlens, cache, prefix, o, workspace, row0, stream)
             self._mlp_tail(i, o, x, ssq, g, stream)
 
     def logits(self, x, ssq, out, stream):

@@ -138,6 +138,50 @@ def decode_attention(q, k, v, lengths, block=64, workspace=None, row0=0):
     return out
 
 
+# ---------------------------------------------------------------- opt-in INT8 prefix KV (analysis.md:95)
+class PrefixKV8:
+    """Int8 copy of the prefix of one layer's cache rows: k8 [rows, S8, 128] / v8t [rows, 128, S8] uint8
+    (excess-128 bytes), sk / sv [rows, 128] float32 per-channel scales.  S8 is rounded up to a multiple of 128."""
+
+    def __init__(self, rows: int, S8: int, device):
+        self.S8 = -(-S8 // 128) * 128
+        self.k8 = torch.zeros(rows, self.S8, 128, dtype=torch.uint8, device=device)
+        self.v8t = torch.zeros(rows, 128, self.S8, dtype=torch.uint8, device=device)
+        self.sk = torch.zeros(rows, 128, dtype=torch.float32, device=device)
+        self.sv = torch.zeros(rows, 128, dtype=torch.float32, device=device)
+
+
+def kv_quantize(k, v, starts, prefix: PrefixKV8, row0=0):
+    """Quantizes positions [0, starts[i]) of cache rows row0 + i of one layer (k/v [B', S, 2, 64] bf16) into
+    prefix: per channel s = max|x| / 127, byte = clamp(rint(x / s), -127, 127) + 128."""
+    assert k.dtype == v.dtype == torch.bfloat16 and k.stride() == v.stride() and k.stride(-1) == 1
+    assert k.shape[2:] == (2, 64) and k.stride(-2) == 64
+    assert starts.dtype == torch.int32 and starts.is_contiguous()
+    call("vk_kv_quantize", _p(k), _p(v), k.shape[0], k.shape[1], k.stride(0), k.stride(1), _p(starts), row0,
+         starts.shape[0], _p(prefix.k8), _p(prefix.v8t), _p(prefix.sk), _p(prefix.sv), prefix.S8, _stream(k))
+
+
+def decode_attention_i8(q, k, v, prefix: PrefixKV8, starts, lengths, max_tail, workspace=None, row0=0):
+    """decode_attention with positions [0, starts[b]) read from the int8 prefix and [starts[b], lengths[b]) from
+    the bf16 cache (0 <= starts < lengths, lengths - starts <= max_tail)."""
+    B, H, D = q.shape
+    assert (H, D) == (8, 64) and q.is_contiguous() and q.dtype == k.dtype == v.dtype == torch.bfloat16
+    assert k.stride() == v.stride() and k.stride(-1) == 1 and k.shape[2:] == (2, 64) and k.stride(-2) == 64
+    assert starts.dtype == lengths.dtype == torch.int32 and starts.shape == lengths.shape == (B,)
+    S = k.shape[1]
+    if workspace is None:
+        key = ("i8", q.device, B, prefix.S8, max_tail)
+        workspace = _WS.get(key)
+        if workspace is None:
+            nbytes = load().vk_decode_attention_i8_workspace_bytes(B, prefix.S8, max_tail)
+            workspace = _WS[key] = torch.zeros(nbytes, dtype=torch.uint8, device=q.device)
+    out = torch.empty_like(q)
+    call("vk_decode_attention_i8", _p(q), _p(k), _p(v), _p(prefix.k8), _p(prefix.v8t), _p(prefix.sk),
+         _p(prefix.sv), _p(starts), _p(lengths), _p(out), B, row0, k.shape[0], S, k.stride(0), k.stride(1),
+         prefix.S8, max_tail, _p(workspace), workspace.numel(), _stream(q))
+    return out
+
+
 def prefill_attention(q, k_cache, v_cache, cu_seqlens, max_seqlen, row0=0, out=None):
     """Varlen causal attention (flash_attn_varlen_func(..., causal=True), viktor/fast_decoder.py:73) over K/V
     already in the cache.  q [n_tok, 8, 64] packed by cu_seqlens [nseq + 1] int32; k_cache/v_cache one layer
