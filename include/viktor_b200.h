@@ -116,7 +116,8 @@ int vk_decode_attention(const void* q, const void* k_cache, const void* v_cache,
  * The prefix of a chunk (its prefilled positions) is written once; an int8 copy halves the bytes decode
  * attention reads for it, while generated tokens stay bf16.  Per channel c of one layer and row (both KV heads,
  * 128 channels): s_c = max_{p < start} |x[p][c]| / 127, stored byte u = clamp(rint(x / s_c), -127, 127) + 128.
- * k8 [cache_rows][S8][128] u8 (position-major), v8t [cache_rows][128][S8] u8 (channel-major), sk/sv
+ * k8 [cache_rows][S8][128] u8 (position-major), v8t [cache_rows][S8 / 128][128][128] u8 (channel-major within
+ * each tile of 128 positions: byte (c, p) of a row at (p / 128) * 16384 + c * 128 + p % 128), sk/sv
  * [cache_rows][128] f32; S8 a multiple of 128. */
 
 /* Quantizes positions [0, starts[i]) (0 <= starts[i] <= min(S, S8), i32) of cache row row0 + i, i < n, of one

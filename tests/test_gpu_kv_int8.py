@@ -48,7 +48,8 @@ def test_kv_quantize_bytes_exact():
     st = torch.tensor(starts, dtype=torch.int32, device=DEV)
     kv_quantize(k, v, st, pre, row0=row0)
     torch.cuda.synchronize()
-    k8, v8t, sk, sv = (t.cpu().numpy() for t in (pre.k8, pre.v8t, pre.sk, pre.sv))
+    k8, sk, sv = (t.cpu().numpy() for t in (pre.k8, pre.sk, pre.sv))
+    v8t = pre.v8t.permute(0, 2, 1, 3).reshape(R, 128, pre.S8).cpu().numpy()  # tiles -> [rows, 128, S8]
     kf = k.float().cpu().numpy().reshape(R, S, 128)
     vf = v.float().cpu().numpy().reshape(R, S, 128)
     for i, s in enumerate(starts):

@@ -314,8 +314,9 @@ VK_DEV void bf16_split(const CUtensorMap* tmK, const CUtensorMap* tmV, const Dec
 
 // ---- int8 split ---------------------------------------------------------------------------------------------------
 // The prefix copy holds excess-128 bytes u = round(x / s_c) + 128 with one scale s_c per channel (both KV heads,
-// 128 channels): K8 position-major [rows][S8][128], V8T channel-major [rows][128][S8].  A 128-position tile is
-// one 16 KB TMA box of each (128-byte swizzle).  The warp MMAs run in fp16: ldmatrix hands each thread four
+// 128 channels): K8 position-major [rows][S8][128], V8T channel-major in tiles of 128 positions,
+// [rows][S8 / 128][128 channels][128 positions], so that a 128-position tile of either is one contiguous 16 KB
+// TMA box (128-byte swizzle).  The warp MMAs run in fp16: ldmatrix hands each thread four
 // consecutive bytes of a row, which two byte permutes and one packed fp16 subtract turn into exact fp16 values
 // (0x6400 | u is 1024 + u; minus 1152 leaves u - 128).  Those four bytes are taken as the k slots
 // {2t, 2t+1, 2t+8, 2t+9} of the MMA fragment; the other operand follows the same order:
@@ -324,6 +325,10 @@ VK_DEV void bf16_split(const CUtensorMap* tmK, const CUtensorMap* tmV, const Dec
 //    pi(r) = {0,1,4,5,8,9,12,13,2,3,6,7,10,11,14,15}[r], which makes the transposed P fragment line up;
 //    the V scales multiply O when the split finishes.
 constexpr int kTile8 = 128;                 // positions per int8 tile
+constexpr int kStages8 = 2;                 // int8 splits: 2 x 32 KB ring (3 measured no faster)
+constexpr int kCombineOff8 = kStages8 * kStageBytes;
+constexpr int kBarOff8 = kCombineOff8 + kCombineBytes;
+constexpr int kSmemBytes8 = (kBarOff8 > kBarOff ? kBarOff8 : kBarOff) + 128 + 1024;  // holds both split layouts
 constexpr int kBox8Bytes = 128 * 128;       // K8: 128 positions x 128 channels; V8T: 128 channels x 128 positions
 static_assert(2 * kBox8Bytes == kStageBytes, "an int8 stage has the size of a bf16 stage");
 
@@ -354,18 +359,18 @@ VK_DEV int i8_chunk(int start, int n8max) {
 
 VK_DEV void i8_split(const CUtensorMap* tmK8, const CUtensorMap* tmV8, const DecodeArgs& a, uint8_t* smem, int b,
                      int p_begin, int p_end, int slot_split, int nsplit) {
-  float* cm = reinterpret_cast<float*>(smem + kCombineOff);
+  float* cm = reinterpret_cast<float*>(smem + kCombineOff8);
   float* cl = cm + 32;
   float* co = cl + 32;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOff);
-  uint64_t* empty = full + kStages;
-  int* last_flag = reinterpret_cast<int*>(empty + kStages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOff8);
+  uint64_t* empty = full + kStages8;
+  int* last_flag = reinterpret_cast<int*>(empty + kStages8);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = (p_end - p_begin + kTile8 - 1) / kTile8;
   const int crow = a.row0 + b;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kStages8; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 4);
     }
@@ -379,9 +384,9 @@ VK_DEV void i8_split(const CUtensorMap* tmK8, const CUtensorMap* tmV8, const Dec
       tma_prefetch_desc(tmV8);
       const uint64_t stream_policy = l2_policy_evict_first();
       for (int t = 0; t < ntiles; ++t) {
-        const int s = t % kStages;
-        const uint32_t ph = (t / kStages) & 1;
-        if (t >= kStages && !mbar_wait(&empty[s], ph ^ 1)) {
+        const int s = t % kStages8;
+        const uint32_t ph = (t / kStages8) & 1;
+        if (t >= kStages8 && !mbar_wait(&empty[s], ph ^ 1)) {
           raise_error(ERR_WAIT_EMPTY);
           break;
         }
@@ -389,7 +394,7 @@ VK_DEV void i8_split(const CUtensorMap* tmK8, const CUtensorMap* tmV8, const Dec
         const int p0 = p_begin + t * kTile8;
         mbar_expect_tx(&full[s], kStageBytes);
         tma_load_3d_hint(st, tmK8, &full[s], 0, p0, crow, stream_policy);
-        tma_load_3d_hint(st + kBox8Bytes, tmV8, &full[s], p0, 0, crow, stream_policy);
+        tma_load_4d_hint(st + kBox8Bytes, tmV8, &full[s], 0, 0, p0 / kTile8, crow, stream_policy);
       }
     }
     return;
@@ -425,8 +430,8 @@ VK_DEV void i8_split(const CUtensorMap* tmK8, const CUtensorMap* tmV8, const Dec
   const int kpos = ((mrow & 6) << 1) | ((mrow >> 3) << 1) | (mrow & 1);   // pi(mrow)
   const int pg = ((g & 6) << 1) | (g & 1);      // pi(g); pi(g + 8) = pg | 2
   for (int t = 0; t < ntiles; ++t) {
-    const int s = t % kStages;
-    const uint32_t ph = (t / kStages) & 1;
+    const int s = t % kStages8;
+    const uint32_t ph = (t / kStages8) & 1;
     if (!mbar_wait(&full[s], ph)) {
       raise_error(ERR_WAIT_FULL);
       break;
@@ -434,10 +439,12 @@ VK_DEV void i8_split(const CUtensorMap* tmK8, const CUtensorMap* tmV8, const Dec
     const uint32_t st = smem_u32(smem + s * kStageBytes);
     const int wp0 = p_begin + t * kTile8 + 32 * warp;   // this warp's 32 positions: two blocks of 16
     // ---- S^T = K8 . Qbd' ----
-    float sc[2][4];
+    // four independent accumulator chains (two blocks x the two KV heads' k steps), summed at the end
+    float sc[2][4], sh[2][2][4];
 #pragma unroll
     for (int sb = 0; sb < 2; ++sb) {
-      sc[sb][0] = sc[sb][1] = sc[sb][2] = sc[sb][3] = 0.f;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) sh[sb][h][0] = sh[sb][h][1] = sh[sb][h][2] = sh[sb][h][3] = 0.f;
       const int row = 32 * warp + 16 * sb + kpos;
 #pragma unroll
       for (int kc = 0; kc < 4; ++kc) {
@@ -445,10 +452,12 @@ VK_DEV void i8_split(const CUtensorMap* tmK8, const CUtensorMap* tmV8, const Dec
         uint32_t r0, r1, r2, r3;
         ldsm_x4(st + row * 128 + ((chunk ^ (row & 7)) << 4), r0, r1, r2, r3);
         const uint32_t a0[4] = {u8_lo(r0), u8_lo(r1), u8_hi(r0), u8_hi(r1)};
-        mma_f16_16816(sc[sb], a0, qb[2 * kc][0], qb[2 * kc][1]);
+        mma_f16_16816(sh[sb][kc >> 1], a0, qb[2 * kc][0], qb[2 * kc][1]);
         const uint32_t a1[4] = {u8_lo(r2), u8_lo(r3), u8_hi(r2), u8_hi(r3)};
-        mma_f16_16816(sc[sb], a1, qb[2 * kc + 1][0], qb[2 * kc + 1][1]);
+        mma_f16_16816(sh[sb][kc >> 1], a1, qb[2 * kc + 1][0], qb[2 * kc + 1][1]);
       }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[sb][e] = sh[sb][0][e] + sh[sb][1][e];
     }
     // ---- online softmax over the warp's 32 positions ----
     float sl[2][4];
@@ -549,7 +558,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   bf16_split(&tmK, &tmV, a, smem, b, L, p_begin, min(p_begin + a.chunk, L), split, (L + a.chunk - 1) / a.chunk);
 }
 
-// int8 prefix + bf16 rest.  CTA (x, b): x < n8max is int8 split x of the prefix [0, starts[b]) (splits of
+// int8 prefix + bf16 rest.  CTA (b, x): x < n8max is int8 split x of the prefix [0, starts[b]) (splits of
 // i8_chunk positions); the others are bf16 splits of chunk positions over [starts[b], L_b).  All splits of a row
 // share its workspace slots (int8 first) and its merge ticket.
 __global__ void __launch_bounds__(kThreads, 2)
@@ -558,15 +567,15 @@ __global__ void __launch_bounds__(kThreads, 2)
                           DecodeArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = aligned_smem(smem_raw);
-  const int b = blockIdx.y, x = blockIdx.x;
+  const int b = blockIdx.x, x = blockIdx.y;  // splits outermost: the long int8 splits start first
   pdl_launch_dependents();
   if (threadIdx.x == 128 && b < a.nq && x < a.n8max) {
     // the int8 prefix is written once, before decoding: warm L2 with this split's first tiles before the wait
     const int p0 = x * i8_chunk(a.S8, a.n8max), crow = a.row0 + b;
-    for (int t = 0; t < kStages; ++t)
+    for (int t = 0; t < kStages8; ++t)
       if (p0 + t * kTile8 < a.S8) {
         tma_prefetch_l2_3d(&tmK8, 0, p0 + t * kTile8, crow);
-        tma_prefetch_l2_3d(&tmV8, p0 + t * kTile8, 0, crow);
+        tma_prefetch_l2_4d(&tmV8, 0, 0, p0 / kTile8 + t, crow);
       }
   }
   pdl_wait();
@@ -594,8 +603,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 // Block (i, which): row row0 + i of one layer's K (which 0) or V (which 1) cache, positions [0, starts[i]).
 // Per channel c: m_c = max |x|, scale s_c = m_c / 127 (0 for an all-zero channel), byte
 // u = clamp(rint(x * (127 / m_c)), -127, 127) + 128 (fp32, round to nearest even).  K8 rows are written
-// position-major; V goes through a shared-memory transpose (128 positions at a time) into channel-major V8T.
-// Positions [starts[i], round_up(starts[i], 128)) of V8T get the byte for 0.
+// position-major; V goes through a shared-memory transpose (128 positions at a time) into the channel-major
+// tiles of V8T.  Positions [starts[i], round_up(starts[i], 128)) of V8T get the byte for 0.
 struct QuantArgs {
   const __nv_bfloat16* k;   // [rows][S][128] bf16 layer cache (element strides stride_kb, stride_ks)
   const __nv_bfloat16* v;
@@ -603,7 +612,7 @@ struct QuantArgs {
   const int32_t* starts;    // [n]
   int row0, n, S, S8;
   uint8_t* k8;              // [rows][S8][128]
-  uint8_t* v8t;             // [rows][128][S8]
+  uint8_t* v8t;             // [rows][S8 / 128][128][128]
   float* sk;                // [rows][128]
   float* sv;
 };
@@ -685,9 +694,10 @@ __global__ void __launch_bounds__(kQuantThreads) kv_quantize_kernel(QuantArgs a)
       }
       __syncthreads();
       const int c = t >> 1, off = (t & 1) * 64;
+      uint8_t* tile = dst + static_cast<int64_t>(p0) * 128;  // the 16 KB tile of positions p0 .. p0 + 127
 #pragma unroll
       for (int k = 0; k < 4; ++k)
-        *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(c) * a.S8 + p0 + off + 16 * k) =
+        *reinterpret_cast<uint4*>(tile + c * 128 + off + 16 * k) =
             *reinterpret_cast<const uint4*>(&tr[c][off + 16 * k]);
       __syncthreads();
     }

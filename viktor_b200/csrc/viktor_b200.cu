@@ -570,10 +570,10 @@ int vk_decode_attention_i8(const void* q, const void* k_cache, const void* v_cac
     if (!make_map_u8(&mk8, k8, 3, dims, strides, box, true)) return VK_ERR_ARG;
   }
   {
-    uint64_t dims[3] = {static_cast<uint64_t>(S8), 128, static_cast<uint64_t>(cache_rows)};
-    uint64_t strides[2] = {static_cast<uint64_t>(S8), static_cast<uint64_t>(S8) * 128};
-    uint32_t box[3] = {attn::kTile8, 128, 1};
-    if (!make_map_u8(&mv8, v8t, 3, dims, strides, box, true)) return VK_ERR_ARG;
+    uint64_t dims[4] = {attn::kTile8, 128, static_cast<uint64_t>(S8 / attn::kTile8), static_cast<uint64_t>(cache_rows)};
+    uint64_t strides[3] = {attn::kTile8, attn::kTile8 * 128, static_cast<uint64_t>(S8) * 128};
+    uint32_t box[4] = {attn::kTile8, 128, 1, 1};
+    if (!make_map_u8(&mv8, v8t, 4, dims, strides, box, true)) return VK_ERR_ARG;
   }
   const int sms = device_sm_count();
   if (sms <= 0) return VK_ERR_CUDA;
@@ -600,9 +600,9 @@ int vk_decode_attention_i8(const void* q, const void* k_cache, const void* v_cac
   a.sk = sk;
   a.sv = sv;
   a.S8 = S8;
-  if (!ensure_smem(attn::decode_attn_i8_kernel, attn::kSmemBytes)) return VK_ERR_CUDA;
-  return launch(attn::decode_attn_i8_kernel, dim3(plan.n8max + plan.n16max, nq), dim3(attn::kThreads),
-                attn::kSmemBytes, stream, 1, mk, mv, mk8, mv8, a);
+  if (!ensure_smem(attn::decode_attn_i8_kernel, attn::kSmemBytes8)) return VK_ERR_CUDA;
+  return launch(attn::decode_attn_i8_kernel, dim3(nq, plan.n8max + plan.n16max), dim3(attn::kThreads),
+                attn::kSmemBytes8, stream, 1, mk, mv, mk8, mv8, a);
 }
 
 }  // extern "C"

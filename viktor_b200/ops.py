@@ -140,13 +140,14 @@ def decode_attention(q, k, v, lengths, block=64, workspace=None, row0=0):
 
 # ---------------------------------------------------------------- opt-in INT8 prefix KV (analysis.md:95)
 class PrefixKV8:
-    """Int8 copy of the prefix of one layer's cache rows: k8 [rows, S8, 128] / v8t [rows, 128, S8] uint8
-    (excess-128 bytes), sk / sv [rows, 128] float32 per-channel scales.  S8 is rounded up to a multiple of 128."""
+    """Int8 copy of the prefix of one layer's cache rows: k8 [rows, S8, 128] / v8t [rows, S8 / 128, 128, 128]
+    uint8 (excess-128 bytes; v8t channel-major within each tile of 128 positions), sk / sv [rows, 128] float32
+    per-channel scales.  S8 is rounded up to a multiple of 128."""
 
     def __init__(self, rows: int, S8: int, device):
         self.S8 = -(-S8 // 128) * 128
         self.k8 = torch.zeros(rows, self.S8, 128, dtype=torch.uint8, device=device)
-        self.v8t = torch.zeros(rows, 128, self.S8, dtype=torch.uint8, device=device)
+        self.v8t = torch.zeros(rows, self.S8 // 128, 128, 128, dtype=torch.uint8, device=device)
         self.sk = torch.zeros(rows, 128, dtype=torch.float32, device=device)
         self.sv = torch.zeros(rows, 128, dtype=torch.float32, device=device)
 
