@@ -639,13 +639,23 @@ __global__ void __launch_bounds__(kQuantThreads) kv_quantize_kernel(QuantArgs a)
   const __nv_bfloat16* src = (which ? a.v : a.k) + static_cast<int64_t>(row) * a.stride_kb;
   const int t = threadIdx.x, cg = t & 15, pr = t >> 4;   // channels 8 cg .. 8 cg + 7, positions pr + 16 k
   float mx[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int p = pr; p < start; p += 16) {
-    const uint4 w = __ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(p) * a.stride_ks + 8 * cg));
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  // eight rows per thread per round, their loads issued together (the pass is bound by load latency)
+  for (int p0 = 0; p0 < start; p0 += 128) {
+    uint4 w[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      mx[2 * e] = fmaxf(mx[2 * e], fabsf(bf16_lo(ws[e])));
-      mx[2 * e + 1] = fmaxf(mx[2 * e + 1], fabsf(bf16_hi(ws[e])));
+    for (int k = 0; k < 8; ++k) {
+      const int p = p0 + pr + 16 * k;
+      w[k] = p < start ? __ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(p) * a.stride_ks + 8 * cg))
+                       : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t ws[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        mx[2 * e] = fmaxf(mx[2 * e], fabsf(bf16_lo(ws[e])));
+        mx[2 * e + 1] = fmaxf(mx[2 * e + 1], fabsf(bf16_hi(ws[e])));
+      }
     }
   }
 #pragma unroll
@@ -664,17 +674,29 @@ __global__ void __launch_bounds__(kQuantThreads) kv_quantize_kernel(QuantArgs a)
   for (int e = 0; e < 8; ++e) inv[e] = inv_s[8 * cg + e];
   if (which == 0) {
     uint8_t* dst = a.k8 + static_cast<int64_t>(row) * a.S8 * 128;
-    for (int p = pr; p < start; p += 16) {
-      const uint4 w = __ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(p) * a.stride_ks + 8 * cg));
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-      uint32_t out[2] = {0u, 0u};
+    for (int p0 = 0; p0 < start; p0 += 128) {
+      uint4 w[8];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const uint32_t lo = quant_byte(bf16_lo(ws[e]), inv[2 * e]);
-        const uint32_t hi = quant_byte(bf16_hi(ws[e]), inv[2 * e + 1]);
-        out[e >> 1] |= (lo | (hi << 8)) << ((e & 1) * 16);
+      for (int k = 0; k < 8; ++k) {
+        const int p = p0 + pr + 16 * k;
+        w[k] = p < start
+                   ? __ldg(reinterpret_cast<const uint4*>(src + static_cast<int64_t>(p) * a.stride_ks + 8 * cg))
+                   : make_uint4(0u, 0u, 0u, 0u);
       }
-      *reinterpret_cast<uint2*>(dst + static_cast<int64_t>(p) * 128 + 8 * cg) = make_uint2(out[0], out[1]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int p = p0 + pr + 16 * k;
+        if (p >= start) break;
+        const uint32_t ws[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
+        uint32_t out[2] = {0u, 0u};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t lo = quant_byte(bf16_lo(ws[e]), inv[2 * e]);
+          const uint32_t hi = quant_byte(bf16_hi(ws[e]), inv[2 * e + 1]);
+          out[e >> 1] |= (lo | (hi << 8)) << ((e & 1) * 16);
+        }
+        *reinterpret_cast<uint2*>(dst + static_cast<int64_t>(p) * 128 + 8 * cg) = make_uint2(out[0], out[1]);
+      }
     }
   } else {
     uint8_t* dst = a.v8t + static_cast<int64_t>(row) * 128 * a.S8;
