@@ -27,3 +27,19 @@ def load(name):
     return dict(meta=meta, cfg=cfg, weights=weights, frames=frames, tokens=z["tokens"],
                 tf_logits=z["tf_logits"], tf_tokens=z["tf_tokens"], bias=z["bias"],
                 noise=z["noise"] if "noise" in z.files else None)
+
+
+def identity_case():
+    """The 128-chunk case of the identity-rate tests: lengths, frames, weights (vocabulary 7, theta 1e6)."""
+    rng = np.random.default_rng(32)
+    lens = [int(v) for v in rng.integers(64, 513, 128)]
+    weights = make_weights(DecoderConfig(vocab_size=7, rope_theta=1e6), seed=31, init="torch")
+    return lens, make_frames(lens, seed=33), weights
+
+
+def load_identity():
+    """identity_b128.npz (tests/golden/make_identity.py): the reference's greedy tokens on identity_case(), with
+    the model in fp32 and in bf16, 32 steps, EOS masked."""
+    z = np.load(os.path.join(HERE, "identity_b128.npz"))
+    return dict(tokens_fp32=z["tokens_fp32"].astype(np.int64), tokens_bf16=z["tokens_bf16"].astype(np.int64),
+                lens=[int(v) for v in z["lens"]])

@@ -147,18 +147,18 @@ def test_full_size_matches_oracle_on_samples(full_size):
 
 
 def test_greedy_chunks_identical_to_oracle_rate():
-    """128 chunks of 64..512 frames, 32 greedy steps against the fp32 oracle (which reproduces the reference's
-    tokens on every golden case).  Every chunk agrees up to its first step whose fp32 top-2 margin is below the
-    bf16 noise floor; with this random (untrained) init such near-ties occur in a few chunks within 32 steps,
-    so the fraction of chunks identical over all steps is measured (0.969 on B200) and held above 0.95."""
+    """128 chunks of 64..512 frames, 32 greedy steps against the fp32 oracle, which reproduces the reference's
+    fp32 tokens on this case for every chunk (tests/golden/identity_b128.npz).  Every chunk agrees up to its first
+    step whose fp32 top-2 margin is below the bf16 noise floor.  Over all 32 steps, with this random (untrained)
+    init, a few chunks meet an fp32 near-tie where any bf16 path may pick the other token: the reference's own
+    bf16 path (its torch engine with the model in bf16) keeps 121 / 128 chunks = 0.945 identical to its fp32
+    tokens, this engine 0.969 (B200).  Held: at least the reference's own bf16 rate, and 0.95."""
+    from golden_io import identity_case, load_identity
     from viktor_b200 import Basecaller, DecodeEngine, DecoderConfig
-    from viktor_b200.synthetic import make_frames, make_weights
-    cfg = DecoderConfig(vocab_size=7, rope_theta=1e6)
-    weights = make_weights(cfg, seed=31, init="torch")
-    rng = np.random.default_rng(32)
-    lens = [int(v) for v in rng.integers(64, 513, 128)]
-    frames = make_frames(lens, seed=33)
+    lens, frames, weights = identity_case()
+    fx = load_identity()
     steps = 32
+    cfg = DecoderConfig(vocab_size=7, rope_theta=1e6)
     model = Basecaller.from_weights(weights, k=1, cfg=cfg)
     eng = DecodeEngine(model, len(lens), steps, max(lens), max_homopolymer=None, device="cuda")
     eng.bias[2] = float("-inf")
@@ -167,11 +167,14 @@ def test_greedy_chunks_identical_to_oracle_rate():
     bias[[0, 1, 2]] = -np.inf
     om = OracleModel(OracleConfig(vocab_size=7, rope_theta=1e6), weights, k=1)
     ref, margin = om.generate(frames, lens, steps, steps=steps, bias=bias, max_homopolymer=None)
+    assert np.array_equal(ref, fx["tokens_fp32"]), "oracle == reference fp32 tokens on this case"
     ok = agree_until_low_margin(got, ref, margin)
     exact = (got == ref).all(1).mean()
-    print(f"identical chunks {exact:.4f} ({(got == ref).all(1).sum()} / {len(lens)})")
+    ref_bf16 = (fx["tokens_bf16"] == fx["tokens_fp32"]).all(1).mean()
+    print(f"identical chunks {exact:.4f} ({(got == ref).all(1).sum()} / {len(lens)}); the reference's own bf16 "
+          f"path: {ref_bf16:.4f}")
     assert ok.all(), np.where(~ok)[0]
-    assert exact >= 0.95
+    assert exact >= ref_bf16 and exact >= 0.95
 
 
 def test_sub_batches_groups_and_empty_prefix():
