@@ -2,7 +2,9 @@
 
 * Teacher-forced logits (all layers over [frames | tokens]) agree with the reference's fp32 logits within
   max-abs 2.5e-2 (bf16 storage between ops, the same rounding points as the reference's Triton path;
-  measured 0.015-0.017 for the 7-token vocabulary, 0.022 for the 343-token 4-mer head).
+  measured 0.015-0.017 for the 7-token vocabulary, 0.022 for the 343-token 4-mer head), and within 1.6x of
+  the error the reference's own modules make in bf16 on the same inputs (0.013-0.020,
+  tests/golden/make_bf16_logits.py).
 * Greedy tokens equal the reference's, per chunk, up to the first step whose fp32 top-2 logit margin is below
   the bf16 noise floor (0.05); from there on a bf16 path may legitimately pick the other token.
 * The CUDA-graph decode equals the eager decode token for token.
@@ -10,11 +12,13 @@
   same tokens inside the full batch as alone) and agree with the oracle on sampled chunks.
 """
 
+import os
+
 import numpy as np
 import pytest
 import torch
 
-from golden_io import load
+from golden_io import HERE as GOLDEN, load
 from oracle import OracleConfig, OracleModel
 
 pytestmark = pytest.mark.gpu
@@ -65,8 +69,10 @@ def test_teacher_forced_logits_match_reference(name):
     got = eng.teacher_forced_logits(torch.from_numpy(g["frames"]), m["lens"],
                                     torch.from_numpy(g["tf_tokens"])).cpu().numpy()
     err = np.abs(got - g["tf_logits"]).max()
-    print(f"{name}: max |logits - reference fp32| = {err:.4f}")
+    ref_bf16 = np.abs(np.load(os.path.join(GOLDEN, "ref_bf16_logits.npz"))[name] - g["tf_logits"]).max()
+    print(f"{name}: max |logits - reference fp32| = {err:.4f} (the reference's own bf16 path: {ref_bf16:.4f})")
     assert err < 2.5e-2, f"max |logits - reference fp32| = {err}"
+    assert err < 1.6 * ref_bf16, f"{err} against the reference's own bf16 error {ref_bf16}"
 
 
 @pytest.mark.parametrize("name", CASES)
