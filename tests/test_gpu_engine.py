@@ -2,7 +2,7 @@
 
 * Teacher-forced logits (all layers over [frames | tokens]) agree with the reference's fp32 logits within
   max-abs 2.5e-2 (bf16 storage between ops, the same rounding points as the reference's Triton path;
-  measured 0.015-0.017 for the 7-token vocabulary, 0.022 for the 343-token 4-mer head), and within 1.6x of
+  measured 0.013-0.016 for the 7-token vocabulary, 0.023 for the 343-token 4-mer head), and within 1.6x of
   the error the reference's own modules make in bf16 on the same inputs (0.013-0.020,
   tests/golden/make_bf16_logits.py).
 * Greedy tokens equal the reference's, per chunk, up to the first step whose fp32 top-2 logit margin is below
