@@ -162,6 +162,104 @@ VK_DEV void finish_split(const DecodeArgs& a, int b, int slot_split, int nsplit,
   if (tid == 0) a.counters[b] = 0;
 }
 
+// ---- bf16 tiles ------------------------------------------------------------------------------------------------
+// Block-diagonal Q operand of sequence b: B[k = (h, d)][n = query head], nonzero where n / 4 == h.
+VK_DEV void bf16_qbd(const DecodeArgs& a, int b, uint32_t (&qb)[8][2]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  const __nv_bfloat16* qp = a.q + static_cast<int64_t>(b) * 512 + g * 64;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const int dbase = (ks & 3) * 16;
+    const bool mine = (g >> 2) == (ks >> 2);
+    qb[ks][0] = mine ? *reinterpret_cast<const uint32_t*>(qp + dbase + 2 * t4) : 0u;
+    qb[ks][1] = mine ? *reinterpret_cast<const uint32_t*>(qp + dbase + 2 * t4 + 8) : 0u;
+  }
+}
+
+// TMA loads of the 64-position bf16 tile at p0 (K and V, both KV heads) into stage st, completing on bar.
+VK_DEV void bf16_load(const CUtensorMap* tmK, const CUtensorMap* tmV, uint64_t* bar, uint8_t* st, int p0, int crow,
+                      uint64_t policy) {
+  mbar_expect_tx(bar, kStageBytes);
+  tma_load_4d_hint(st, tmK, bar, 0, 0, p0, crow, policy);
+  tma_load_4d_hint(st + kBoxBytes, tmK, bar, 0, 1, p0, crow, policy);
+  tma_load_4d_hint(st + 2 * kBoxBytes, tmV, bar, 0, 0, p0, crow, policy);
+  tma_load_4d_hint(st + 3 * kBoxBytes, tmV, bar, 0, 1, p0, crow, policy);
+}
+
+// Online-softmax update of (m, l, o) over this warp's 16 positions of the bf16 tile staged at st (positions
+// tile_p0 .. tile_p0 + 63; those at or past L are masked).
+VK_DEV void bf16_tile(uint32_t st, int tile_p0, int L, float scale_log2, const uint32_t (&qb)[8][2], float& m0,
+                      float& m1, float& l0, float& l1, float (&o)[8][4]) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int j = lane >> 3, rr = lane & 7;
+  // ---- S^T = K . Qbd ----
+  float sc[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    const int row = 16 * warp + (j & 1) * 8 + rr;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint32_t base = st + (ks >> 2) * kBoxBytes;
+      const int chunk = (ks & 3) * 2 + (j >> 1);
+      uint32_t af[4];
+      ldsm_x4(base + row * 128 + ((chunk ^ (row & 7)) << 4), af[0], af[1], af[2], af[3]);
+      mma_bf16_16816(sc, af, qb[ks][0], qb[ks][1]);
+    }
+  }
+  // ---- online softmax over this warp's 16 positions ----
+  const int pa = tile_p0 + 16 * warp + g, pb = pa + 8;
+  const float s00 = pa < L ? sc[0] * scale_log2 : -INFINITY;
+  const float s01 = pa < L ? sc[1] * scale_log2 : -INFINITY;
+  const float s10 = pb < L ? sc[2] * scale_log2 : -INFINITY;
+  const float s11 = pb < L ? sc[3] * scale_log2 : -INFINITY;
+  float tm0 = fmaxf(s00, s10), tm1 = fmaxf(s01, s11);
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, off));
+    tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, off));
+  }
+  const float mn0 = fmaxf(m0, tm0), mn1 = fmaxf(m1, tm1);
+  const float mu0 = mn0 == -INFINITY ? 0.f : mn0, mu1 = mn1 == -INFINITY ? 0.f : mn1;
+  const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
+  const float p00 = exp2f(s00 - mu0), p10 = exp2f(s10 - mu0);
+  const float p01 = exp2f(s01 - mu1), p11 = exp2f(s11 - mu1);
+  l0 = l0 * al0 + p00 + p10;
+  l1 = l1 * al1 + p01 + p11;
+  m0 = mn0;
+  m1 = mn1;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    o[i][0] *= al0;
+    o[i][2] *= al0;
+    o[i][1] *= al1;
+    o[i][3] *= al1;
+  }
+  const uint32_t pb0 = movmatrix_t(pack_bf16x2(p00, p01));
+  const uint32_t pb1 = movmatrix_t(pack_bf16x2(p10, p11));
+  // ---- O^T += V^T . P^T ----
+  const bool partial = tile_p0 + kTile > L;
+  const int kp = tile_p0 + 16 * warp + 2 * t4;
+  const uint32_t mk0 = (kp < L ? 0x0000FFFFu : 0u) | (kp + 1 < L ? 0xFFFF0000u : 0u);
+  const uint32_t mk1 = (kp + 8 < L ? 0x0000FFFFu : 0u) | (kp + 9 < L ? 0xFFFF0000u : 0u);
+  {
+    const int prow = 16 * warp + (j >> 1) * 8 + rr;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const uint32_t base = st + (2 + (mt >> 2)) * kBoxBytes;
+      const int chunk = (mt & 3) * 2 + (j & 1);
+      uint32_t af[4];
+      ldsm_x4_t(base + prow * 128 + ((chunk ^ (prow & 7)) << 4), af[0], af[1], af[2], af[3]);
+      if (partial) {  // rows past the sequence may hold stale data: zero them, not just their weights
+        af[0] &= mk0;
+        af[1] &= mk0;
+        af[2] &= mk1;
+        af[3] &= mk1;
+      }
+      mma_bf16_16816(o[mt], af, pb0, pb1);
+    }
+  }
+}
+
 // ---- bf16 split -------------------------------------------------------------------------------------------------
 // Positions [p_begin, p_end) of row b (both KV heads, all 8 query heads) from the bf16 cache; the partial result
 // goes to workspace slot slot_split of the row's nsplit.  p_begin + chunk >= p_end and chunk is a multiple of
@@ -199,38 +297,19 @@ VK_DEV void bf16_split(const CUtensorMap* tmK, const CUtensorMap* tmV, const Dec
           raise_error(ERR_WAIT_EMPTY);
           break;
         }
-        uint8_t* st = smem + s * kStageBytes;
-        const int p0 = p_begin + t * kTile;
-        mbar_expect_tx(&full[s], kStageBytes);
-        tma_load_4d_hint(st, tmK, &full[s], 0, 0, p0, crow, stream_policy);
-        tma_load_4d_hint(st + kBoxBytes, tmK, &full[s], 0, 1, p0, crow, stream_policy);
-        tma_load_4d_hint(st + 2 * kBoxBytes, tmV, &full[s], 0, 0, p0, crow, stream_policy);
-        tma_load_4d_hint(st + 3 * kBoxBytes, tmV, &full[s], 0, 1, p0, crow, stream_policy);
+        bf16_load(tmK, tmV, &full[s], smem + s * kStageBytes, p_begin + t * kTile, crow, stream_policy);
       }
     }
     return;
   }
 
   // ---------------- compute warps 0..3 ----------------
-  const int g = lane >> 2, t4 = lane & 3;
-  // Block-diagonal Q operand: B[k = (h, d)][n = query head], nonzero where n / 4 == h.
   uint32_t qb[8][2];
-  {
-    const __nv_bfloat16* qp = a.q + static_cast<int64_t>(b) * 512 + g * 64;
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const int dbase = (ks & 3) * 16;
-      const bool mine = (g >> 2) == (ks >> 2);
-      qb[ks][0] = mine ? *reinterpret_cast<const uint32_t*>(qp + dbase + 2 * t4) : 0u;
-      qb[ks][1] = mine ? *reinterpret_cast<const uint32_t*>(qp + dbase + 2 * t4 + 8) : 0u;
-    }
-  }
+  bf16_qbd(a, b, qb);
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // heads 2*t4, 2*t4 + 1
   float o[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-
-  const int j = lane >> 3, rr = lane & 7;
   for (int t = 0; t < ntiles; ++t) {
     const int s = t % kStages;
     const uint32_t ph = (t / kStages) & 1;
@@ -238,73 +317,7 @@ VK_DEV void bf16_split(const CUtensorMap* tmK, const CUtensorMap* tmV, const Dec
       raise_error(ERR_WAIT_FULL);
       break;
     }
-    const uint32_t st = smem_u32(smem + s * kStageBytes);
-    const int tile_p0 = p_begin + t * kTile;
-    // ---- S^T = K . Qbd ----
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
-    {
-      const int row = 16 * warp + (j & 1) * 8 + rr;
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t base = st + (ks >> 2) * kBoxBytes;
-        const int chunk = (ks & 3) * 2 + (j >> 1);
-        uint32_t af[4];
-        ldsm_x4(base + row * 128 + ((chunk ^ (row & 7)) << 4), af[0], af[1], af[2], af[3]);
-        mma_bf16_16816(sc, af, qb[ks][0], qb[ks][1]);
-      }
-    }
-    // ---- online softmax over this warp's 16 positions ----
-    const int pa = tile_p0 + 16 * warp + g, pb = pa + 8;
-    const float s00 = pa < L ? sc[0] * a.scale_log2 : -INFINITY;
-    const float s01 = pa < L ? sc[1] * a.scale_log2 : -INFINITY;
-    const float s10 = pb < L ? sc[2] * a.scale_log2 : -INFINITY;
-    const float s11 = pb < L ? sc[3] * a.scale_log2 : -INFINITY;
-    float tm0 = fmaxf(s00, s10), tm1 = fmaxf(s01, s11);
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-      tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, off));
-      tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, off));
-    }
-    const float mn0 = fmaxf(m0, tm0), mn1 = fmaxf(m1, tm1);
-    const float mu0 = mn0 == -INFINITY ? 0.f : mn0, mu1 = mn1 == -INFINITY ? 0.f : mn1;
-    const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
-    const float p00 = exp2f(s00 - mu0), p10 = exp2f(s10 - mu0);
-    const float p01 = exp2f(s01 - mu1), p11 = exp2f(s11 - mu1);
-    l0 = l0 * al0 + p00 + p10;
-    l1 = l1 * al1 + p01 + p11;
-    m0 = mn0;
-    m1 = mn1;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      o[i][0] *= al0;
-      o[i][2] *= al0;
-      o[i][1] *= al1;
-      o[i][3] *= al1;
-    }
-    const uint32_t pb0 = movmatrix_t(pack_bf16x2(p00, p01));
-    const uint32_t pb1 = movmatrix_t(pack_bf16x2(p10, p11));
-    // ---- O^T += V^T . P^T ----
-    const bool partial = tile_p0 + kTile > L;
-    const int kp = tile_p0 + 16 * warp + 2 * t4;
-    const uint32_t mk0 = (kp < L ? 0x0000FFFFu : 0u) | (kp + 1 < L ? 0xFFFF0000u : 0u);
-    const uint32_t mk1 = (kp + 8 < L ? 0x0000FFFFu : 0u) | (kp + 9 < L ? 0xFFFF0000u : 0u);
-    {
-      const int prow = 16 * warp + (j >> 1) * 8 + rr;
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        const uint32_t base = st + (2 + (mt >> 2)) * kBoxBytes;
-        const int chunk = (mt & 3) * 2 + (j & 1);
-        uint32_t af[4];
-        ldsm_x4_t(base + prow * 128 + ((chunk ^ (prow & 7)) << 4), af[0], af[1], af[2], af[3]);
-        if (partial) {  // rows past the sequence may hold stale data: zero them, not just their weights
-          af[0] &= mk0;
-          af[1] &= mk0;
-          af[2] &= mk1;
-          af[3] &= mk1;
-        }
-        mma_bf16_16816(o[mt], af, pb0, pb1);
-      }
-    }
+    bf16_tile(smem_u32(smem + s * kStageBytes), p_begin + t * kTile, L, a.scale_log2, qb, m0, m1, l0, l1, o);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
@@ -357,6 +370,125 @@ VK_DEV int i8_chunk(int start, int n8max) {
   return (per + kTile8 - 1) / kTile8 * kTile8;
 }
 
+// Qbd' of sequence b (cache row crow), fp16.
+VK_DEV void i8_qbd(const DecodeArgs& a, int b, int crow, uint32_t (&qb)[8][2]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  // Qbd' in fp16: k step ks covers channels 16 ks .. 16 ks + 15 (KV head ks / 4); this thread's k slots 2 t4,
+  // 2 t4 + 1 hold channels 4 t4, 4 t4 + 1 and slots 2 t4 + 8, 2 t4 + 9 channels 4 t4 + 2, 4 t4 + 3.
+  const __nv_bfloat16* qp = a.q + static_cast<int64_t>(b) * 512 + g * 64;
+  const float* skp = a.sk + static_cast<int64_t>(crow) * 128 + (g >> 2) * 64;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const int d0 = (ks & 3) * 16 + 4 * t4;
+    if ((g >> 2) == (ks >> 2)) {
+      const uint2 qv = *reinterpret_cast<const uint2*>(qp + d0);
+      const float4 scl = *reinterpret_cast<const float4*>(skp + d0);
+      qb[ks][0] = pack_f16x2(bf16_lo(qv.x) * scl.x, bf16_hi(qv.x) * scl.y);
+      qb[ks][1] = pack_f16x2(bf16_lo(qv.y) * scl.z, bf16_hi(qv.y) * scl.w);
+    } else {
+      qb[ks][0] = qb[ks][1] = 0u;
+    }
+  }
+}
+
+// TMA loads of the 128-position int8 tile at p0 (one 16 KB box of K8 and one of V8T) into stage st.
+VK_DEV void i8_load(const CUtensorMap* tmK8, const CUtensorMap* tmV8, uint64_t* bar, uint8_t* st, int p0, int crow,
+                    uint64_t policy) {
+  mbar_expect_tx(bar, kStageBytes);
+  tma_load_3d_hint(st, tmK8, bar, 0, p0, crow, policy);
+  tma_load_4d_hint(st + kBox8Bytes, tmV8, bar, 0, 0, p0 / kTile8, crow, policy);
+}
+
+// Online-softmax update of (m, l, o) over this warp's 32 positions of the int8 tile staged at st (positions
+// tile_p0 .. tile_p0 + 127; those at or past p_end are masked).
+VK_DEV void i8_tile(uint32_t st, int tile_p0, int p_end, float scale_log2, const uint32_t (&qb)[8][2], float& m0,
+                    float& m1, float& l0, float& l1, float (&o)[8][4]) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2;
+  const int j = lane >> 3, rr = lane & 7;       // ldmatrix: this lane addresses row rr of matrix j
+  const int mrow = rr + (j & 1) * 8;            // MMA row of that address (matrices: rows 0-7, 8-15, 0-7, 8-15)
+  const int kpos = ((mrow & 6) << 1) | ((mrow >> 3) << 1) | (mrow & 1);   // pi(mrow)
+  const int pg = ((g & 6) << 1) | (g & 1);      // pi(g); pi(g + 8) = pg | 2
+  const int wp0 = tile_p0 + 32 * warp;   // this warp's 32 positions: two blocks of 16
+  // ---- S^T = K8 . Qbd' ----
+  // four independent accumulator chains (two blocks x the two KV heads' k steps), summed at the end
+  float sc[2][4], sh[2][2][4];
+#pragma unroll
+  for (int sb = 0; sb < 2; ++sb) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) sh[sb][h][0] = sh[sb][h][1] = sh[sb][h][2] = sh[sb][h][3] = 0.f;
+    const int row = 32 * warp + 16 * sb + kpos;
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc) {
+      const int chunk = 2 * kc + (j >> 1);
+      uint32_t r0, r1, r2, r3;
+      ldsm_x4(st + row * 128 + ((chunk ^ (row & 7)) << 4), r0, r1, r2, r3);
+      const uint32_t a0[4] = {u8_lo(r0), u8_lo(r1), u8_hi(r0), u8_hi(r1)};
+      mma_f16_16816(sh[sb][kc >> 1], a0, qb[2 * kc][0], qb[2 * kc][1]);
+      const uint32_t a1[4] = {u8_lo(r2), u8_lo(r3), u8_hi(r2), u8_hi(r3)};
+      mma_f16_16816(sh[sb][kc >> 1], a1, qb[2 * kc + 1][0], qb[2 * kc + 1][1]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sc[sb][e] = sh[sb][0][e] + sh[sb][1][e];
+  }
+  // ---- online softmax over the warp's 32 positions ----
+  float sl[2][4];
+#pragma unroll
+  for (int sb = 0; sb < 2; ++sb) {
+    const int pa = wp0 + 16 * sb + pg, pb = pa + 2;
+    sl[sb][0] = pa < p_end ? sc[sb][0] * scale_log2 : -INFINITY;
+    sl[sb][1] = pa < p_end ? sc[sb][1] * scale_log2 : -INFINITY;
+    sl[sb][2] = pb < p_end ? sc[sb][2] * scale_log2 : -INFINITY;
+    sl[sb][3] = pb < p_end ? sc[sb][3] * scale_log2 : -INFINITY;
+  }
+  float tm0 = fmaxf(fmaxf(sl[0][0], sl[0][2]), fmaxf(sl[1][0], sl[1][2]));
+  float tm1 = fmaxf(fmaxf(sl[0][1], sl[0][3]), fmaxf(sl[1][1], sl[1][3]));
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, off));
+    tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, off));
+  }
+  const float mn0 = fmaxf(m0, tm0), mn1 = fmaxf(m1, tm1);
+  const float mu0 = mn0 == -INFINITY ? 0.f : mn0, mu1 = mn1 == -INFINITY ? 0.f : mn1;
+  const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
+  uint32_t pfrag[2][2];
+  float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+  for (int sb = 0; sb < 2; ++sb) {
+    const float p00 = exp2f(sl[sb][0] - mu0), p10 = exp2f(sl[sb][2] - mu0);
+    const float p01 = exp2f(sl[sb][1] - mu1), p11 = exp2f(sl[sb][3] - mu1);
+    ls0 += p00 + p10;
+    ls1 += p01 + p11;
+    pfrag[sb][0] = movmatrix_t(pack_f16x2(p00, p01));
+    pfrag[sb][1] = movmatrix_t(pack_f16x2(p10, p11));
+  }
+  l0 = l0 * al0 + ls0;
+  l1 = l1 * al1 + ls1;
+  m0 = mn0;
+  m1 = mn1;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    o[i][0] *= al0;
+    o[i][2] *= al0;
+    o[i][1] *= al1;
+    o[i][3] *= al1;
+  }
+  // ---- O^T += V8T . P^T (positions past the prefix have P = 0 and finite bytes) ----
+  {
+    const int vchunk = 2 * warp + (j >> 1);   // matrices: (channels 0-7, block 0), (8-15, 0), (0-7, 1), (8-15, 1)
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const int ch = 16 * mt + mrow;
+      uint32_t r0, r1, r2, r3;
+      ldsm_x4(st + kBox8Bytes + ch * 128 + ((vchunk ^ (ch & 7)) << 4), r0, r1, r2, r3);
+      const uint32_t a0[4] = {u8_lo(r0), u8_lo(r1), u8_hi(r0), u8_hi(r1)};
+      mma_f16_16816(o[mt], a0, pfrag[0][0], pfrag[0][1]);
+      const uint32_t a1[4] = {u8_lo(r2), u8_lo(r3), u8_hi(r2), u8_hi(r3)};
+      mma_f16_16816(o[mt], a1, pfrag[1][0], pfrag[1][1]);
+    }
+  }
+}
+
 VK_DEV void i8_split(const CUtensorMap* tmK8, const CUtensorMap* tmV8, const DecodeArgs& a, uint8_t* smem, int b,
                      int p_begin, int p_end, int slot_split, int nsplit) {
   float* cm = reinterpret_cast<float*>(smem + kCombineOff8);
@@ -390,45 +522,18 @@ VK_DEV void i8_split(const CUtensorMap* tmK8, const CUtensorMap* tmV8, const Dec
           raise_error(ERR_WAIT_EMPTY);
           break;
         }
-        uint8_t* st = smem + s * kStageBytes;
-        const int p0 = p_begin + t * kTile8;
-        mbar_expect_tx(&full[s], kStageBytes);
-        tma_load_3d_hint(st, tmK8, &full[s], 0, p0, crow, stream_policy);
-        tma_load_4d_hint(st + kBox8Bytes, tmV8, &full[s], 0, 0, p0 / kTile8, crow, stream_policy);
+        i8_load(tmK8, tmV8, &full[s], smem + s * kStageBytes, p_begin + t * kTile8, crow, stream_policy);
       }
     }
     return;
   }
 
-  const int g = lane >> 2, t4 = lane & 3;
-  // Qbd' in fp16: k step ks covers channels 16 ks .. 16 ks + 15 (KV head ks / 4); this thread's k slots 2 t4,
-  // 2 t4 + 1 hold channels 4 t4, 4 t4 + 1 and slots 2 t4 + 8, 2 t4 + 9 channels 4 t4 + 2, 4 t4 + 3.
   uint32_t qb[8][2];
-  {
-    const __nv_bfloat16* qp = a.q + static_cast<int64_t>(b) * 512 + g * 64;
-    const float* skp = a.sk + static_cast<int64_t>(crow) * 128 + (g >> 2) * 64;
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const int d0 = (ks & 3) * 16 + 4 * t4;
-      if ((g >> 2) == (ks >> 2)) {
-        const uint2 qv = *reinterpret_cast<const uint2*>(qp + d0);
-        const float4 scl = *reinterpret_cast<const float4*>(skp + d0);
-        qb[ks][0] = pack_f16x2(bf16_lo(qv.x) * scl.x, bf16_hi(qv.x) * scl.y);
-        qb[ks][1] = pack_f16x2(bf16_lo(qv.y) * scl.z, bf16_hi(qv.y) * scl.w);
-      } else {
-        qb[ks][0] = qb[ks][1] = 0u;
-      }
-    }
-  }
+  i8_qbd(a, b, crow, qb);
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   float o[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-
-  const int j = lane >> 3, rr = lane & 7;       // ldmatrix: this lane addresses row rr of matrix j
-  const int mrow = rr + (j & 1) * 8;            // MMA row of that address (matrices: rows 0-7, 8-15, 0-7, 8-15)
-  const int kpos = ((mrow & 6) << 1) | ((mrow >> 3) << 1) | (mrow & 1);   // pi(mrow)
-  const int pg = ((g & 6) << 1) | (g & 1);      // pi(g); pi(g + 8) = pg | 2
   for (int t = 0; t < ntiles; ++t) {
     const int s = t % kStages8;
     const uint32_t ph = (t / kStages8) & 1;
@@ -436,85 +541,7 @@ VK_DEV void i8_split(const CUtensorMap* tmK8, const CUtensorMap* tmV8, const Dec
       raise_error(ERR_WAIT_FULL);
       break;
     }
-    const uint32_t st = smem_u32(smem + s * kStageBytes);
-    const int wp0 = p_begin + t * kTile8 + 32 * warp;   // this warp's 32 positions: two blocks of 16
-    // ---- S^T = K8 . Qbd' ----
-    // four independent accumulator chains (two blocks x the two KV heads' k steps), summed at the end
-    float sc[2][4], sh[2][2][4];
-#pragma unroll
-    for (int sb = 0; sb < 2; ++sb) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h) sh[sb][h][0] = sh[sb][h][1] = sh[sb][h][2] = sh[sb][h][3] = 0.f;
-      const int row = 32 * warp + 16 * sb + kpos;
-#pragma unroll
-      for (int kc = 0; kc < 4; ++kc) {
-        const int chunk = 2 * kc + (j >> 1);
-        uint32_t r0, r1, r2, r3;
-        ldsm_x4(st + row * 128 + ((chunk ^ (row & 7)) << 4), r0, r1, r2, r3);
-        const uint32_t a0[4] = {u8_lo(r0), u8_lo(r1), u8_hi(r0), u8_hi(r1)};
-        mma_f16_16816(sh[sb][kc >> 1], a0, qb[2 * kc][0], qb[2 * kc][1]);
-        const uint32_t a1[4] = {u8_lo(r2), u8_lo(r3), u8_hi(r2), u8_hi(r3)};
-        mma_f16_16816(sh[sb][kc >> 1], a1, qb[2 * kc + 1][0], qb[2 * kc + 1][1]);
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) sc[sb][e] = sh[sb][0][e] + sh[sb][1][e];
-    }
-    // ---- online softmax over the warp's 32 positions ----
-    float sl[2][4];
-#pragma unroll
-    for (int sb = 0; sb < 2; ++sb) {
-      const int pa = wp0 + 16 * sb + pg, pb = pa + 2;
-      sl[sb][0] = pa < p_end ? sc[sb][0] * a.scale_log2 : -INFINITY;
-      sl[sb][1] = pa < p_end ? sc[sb][1] * a.scale_log2 : -INFINITY;
-      sl[sb][2] = pb < p_end ? sc[sb][2] * a.scale_log2 : -INFINITY;
-      sl[sb][3] = pb < p_end ? sc[sb][3] * a.scale_log2 : -INFINITY;
-    }
-    float tm0 = fmaxf(fmaxf(sl[0][0], sl[0][2]), fmaxf(sl[1][0], sl[1][2]));
-    float tm1 = fmaxf(fmaxf(sl[0][1], sl[0][3]), fmaxf(sl[1][1], sl[1][3]));
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-      tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, off));
-      tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, off));
-    }
-    const float mn0 = fmaxf(m0, tm0), mn1 = fmaxf(m1, tm1);
-    const float mu0 = mn0 == -INFINITY ? 0.f : mn0, mu1 = mn1 == -INFINITY ? 0.f : mn1;
-    const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
-    uint32_t pfrag[2][2];
-    float ls0 = 0.f, ls1 = 0.f;
-#pragma unroll
-    for (int sb = 0; sb < 2; ++sb) {
-      const float p00 = exp2f(sl[sb][0] - mu0), p10 = exp2f(sl[sb][2] - mu0);
-      const float p01 = exp2f(sl[sb][1] - mu1), p11 = exp2f(sl[sb][3] - mu1);
-      ls0 += p00 + p10;
-      ls1 += p01 + p11;
-      pfrag[sb][0] = movmatrix_t(pack_f16x2(p00, p01));
-      pfrag[sb][1] = movmatrix_t(pack_f16x2(p10, p11));
-    }
-    l0 = l0 * al0 + ls0;
-    l1 = l1 * al1 + ls1;
-    m0 = mn0;
-    m1 = mn1;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      o[i][0] *= al0;
-      o[i][2] *= al0;
-      o[i][1] *= al1;
-      o[i][3] *= al1;
-    }
-    // ---- O^T += V8T . P^T (positions past the prefix have P = 0 and finite bytes) ----
-    {
-      const int vchunk = 2 * warp + (j >> 1);   // matrices: (channels 0-7, block 0), (8-15, 0), (0-7, 1), (8-15, 1)
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        const int ch = 16 * mt + mrow;
-        uint32_t r0, r1, r2, r3;
-        ldsm_x4(st + kBox8Bytes + ch * 128 + ((vchunk ^ (ch & 7)) << 4), r0, r1, r2, r3);
-        const uint32_t a0[4] = {u8_lo(r0), u8_lo(r1), u8_hi(r0), u8_hi(r1)};
-        mma_f16_16816(o[mt], a0, pfrag[0][0], pfrag[0][1]);
-        const uint32_t a1[4] = {u8_lo(r2), u8_lo(r3), u8_hi(r2), u8_hi(r3)};
-        mma_f16_16816(o[mt], a1, pfrag[1][0], pfrag[1][1]);
-      }
-    }
+    i8_tile(smem_u32(smem + s * kStageBytes), p_begin + t * kTile8, p_end, a.scale_log2, qb, m0, m1, l0, l1, o);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
