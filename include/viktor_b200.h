@@ -146,9 +146,9 @@ int vk_decode_attention_i8(const void* q, const void* k_cache, const void* v_cac
  * Limits: nq <= 256 queries and S <= 4096 cache positions; larger requests return VK_ERR_ARG with a message on
  * stderr.  The array (8.25 MiB) lives on every GPU that loads the library until the process exits.  The first
  * call on a device looks up the array's device address; make that first call before any stream capture.
- * Every call clears the per-query tickets it uses and then shares the array with all other calls: calls whose
- * executions overlap on the GPU (concurrent streams, or several devices' work racing on one array per device)
- * corrupt each other's results — issue them in order on one stream per device. */
+ * Every call clears the per-query tickets it uses and then shares the device's array with all other calls on
+ * that device: calls whose executions overlap on the same GPU (for example on concurrent streams) corrupt each
+ * other's results — issue them in order on one stream per device.  Each device has its own array. */
 int vk_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, const int32_t* lengths,
                                 void* out, int nq, int row0, int cache_rows, int S, int64_t stride_kb,
                                 int64_t stride_ks, void* stream);
