@@ -171,3 +171,28 @@ def test_engine_int8_prefix_tokens():
           f"agree-until-margin {ok.mean():.4f}")
     assert ok.all(), np.where(~ok)[0]
     assert exact >= 0.9
+
+
+@pytest.mark.parametrize("name", ["base_theta1e6", "base_theta1e4", "kmer4", "homopolymer", "pos_scale2", "base_b8"])
+def test_engine_int8_prefix_golden_cases(name):
+    """kv_int8=True on the golden cases (4-mer vocabulary and its tail rule, homopolymer stop, pos_scale 2, ragged
+    batch of 8): the reference's greedy tokens, up to each row's first step whose fp32 top-2 margin is below 0.1
+    (the int8 mode's floor)."""
+    from golden_io import load
+    from oracle import OracleConfig, OracleModel
+    from viktor_b200 import Basecaller, DecodeEngine, DecoderConfig
+    g = load(name)
+    m = g["meta"]
+    model = Basecaller.from_weights(g["weights"], k=m["k"], cfg=DecoderConfig(**m["cfg"]), d_enc=m["d_enc"],
+                                    pos_scale=m["pos_scale"])
+    eng = DecodeEngine(model, len(m["lens"]), m["max_new"], max(m["lens"]), max_homopolymer=m["max_homopolymer"],
+                       device="cuda", kv_int8=True)
+    eng.bias.copy_(torch.from_numpy(g["bias"]))
+    got = eng.generate(torch.from_numpy(g["frames"]), m["lens"], m["max_new"]).cpu().numpy()
+    eng.check_errors()
+    om = OracleModel(OracleConfig(**m["cfg"]), g["weights"], k=m["k"], pos_scale=m["pos_scale"])
+    _, margin = om.generate(g["frames"], m["lens"], m["max_new"], steps=m["max_new"], bias=g["bias"],
+                            max_homopolymer=m["max_homopolymer"])
+    ok = _agree_until_low_margin(got, g["tokens"], margin, 0.1)
+    print(f"{name}: kv_int8 identical rows {(got == g['tokens']).all(1).mean():.3f}")
+    assert ok.all(), f"rows disagreeing before a low-margin step: {np.where(~ok)[0]}"
