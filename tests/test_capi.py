@@ -52,3 +52,45 @@ def test_argument_errors_are_status_codes():
                                     None, None, fake, 7, t, None) == _lib.VK_ERR_ARG
     assert lib.vk_sample_update(fake, 7, fake, fake, fake, 0, *ptrs, 4, 4, fake, fake, fake, 2, 7, 2, 0, None,
                                 None, None, fake, 6, 0.7, None) == _lib.VK_ERR_ARG  # ld_noise < V
+
+
+def test_int8_prefix_entry_points_validate_arguments():
+    """The int8 prefix entry points: workspace sizing (host only) and argument checks that fail before any
+    device access (S8 a multiple of 128, 0 < max_tail <= S, the workspace large enough, no null pointers)."""
+    lib = _lib.load()
+    w = lib.vk_decode_attention_i8_workspace_bytes(128, 2176, 1101)
+    assert w > 0 and lib.vk_decode_attention_i8_workspace_bytes(128, 2176, 2202) > w
+    assert lib.vk_decode_attention_i8_workspace_bytes(0, 2176, 1101) == 0
+    fake = 16  # any 16-byte-aligned non-null address: validation fails before anything is dereferenced
+    S, rows = 3200, 128
+
+    def attn(S8=2176, max_tail=1101, ws_bytes=w, q=fake):
+        return lib.vk_decode_attention_i8(q, fake, fake, fake, fake, fake, fake, fake, fake, fake, rows, 0, rows, S,
+                                          S * 128, 128, S8, max_tail, fake, ws_bytes, None)
+
+    assert attn(S8=2100) == _lib.VK_ERR_ARG          # not a multiple of 128
+    assert attn(max_tail=0) == _lib.VK_ERR_ARG
+    assert attn(max_tail=S + 1) == _lib.VK_ERR_ARG
+    assert attn(ws_bytes=w - 1) == _lib.VK_ERR_ARG   # workspace too small
+    assert attn(q=None) == _lib.VK_ERR_ARG
+    assert lib.vk_kv_quantize(fake, fake, rows, S, S * 128, 128, fake, 0, rows, fake, fake, fake, fake, 2100,
+                              None) == _lib.VK_ERR_ARG
+    assert lib.vk_kv_quantize(fake, fake, rows, S, S * 128, 128, None, 0, rows, fake, fake, fake, fake, 2176,
+                              None) == _lib.VK_ERR_ARG
+    assert lib.vk_kv_quantize(fake, fake, rows, S, S * 128, 128, fake, 1, rows, fake, fake, fake, fake, 2176,
+                              None) == _lib.VK_ERR_ARG  # rows past the cache
+    assert lib.vk_kv_quantize(None, None, 0, 0, 0, 0, None, 0, 0, None, None, None, None, 0, None) == _lib.VK_OK
+
+
+def test_stitch_entry_points_validate_arguments():
+    lib = _lib.load()
+    out = (_lib.C.c_int * 3)()
+    assert lib.vk_align(None, 3, b"ACG", 3, 0, -1, out, None, 0) == _lib.VK_ERR_ARG
+    assert lib.vk_align(b"ACG", 3, b"ACG", 3, 3, -1, out, None, 0) == _lib.VK_ERR_ARG  # unknown mode
+    buf = _lib.C.create_string_buffer(4)
+    assert lib.vk_align(b"ACG", 3, b"ACG", 3, 0, -1, out, buf, 4) == _lib.VK_ERR_ARG  # CIGAR buffer too small
+    cut = (_lib.C.c_int * 2)()
+    assert lib.vk_overlap_cut(None, 5, b"ACGTA", 5, 10, 1.0, cut) == _lib.VK_ERR_ARG
+    n = _lib.C.c_int64(0)
+    assert lib.vk_stitch(None, None, None, 2, 6, None, 0, _lib.C.byref(n)) == _lib.VK_ERR_ARG
+    assert lib.vk_stitch(None, None, None, 0, 6, None, 0, _lib.C.byref(n)) == _lib.VK_OK and n.value == 0
