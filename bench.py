@@ -123,17 +123,17 @@ def make_lens(cfg, B, seed):
     return [PLEN] * B if cfg["frames"] == "full" else varlen_prefix_lengths(B, seed=seed)
 
 
-def cpu_baseline(args, cfg):
+def cpu_baseline(args, cfg, steps=None):
     """The reference path on the host cores: a multithreaded PyTorch-CPU fp32 restatement (oracle/decoder_torch.py,
     pinned to the reference's golden tokens) on a bounded sample of the same workload: 4 chunks x 2048 frames,
-    prefill + the workload's full number of greedy steps."""
+    prefill + the workload's full number of greedy steps (or `steps`)."""
     import torch
     from oracle import OracleConfig
     from oracle.decoder_torch import TorchCPUModel
     from viktor_b200.config import DecoderConfig
     from viktor_b200.synthetic import make_frames, make_weights
     B = 4
-    steps = args.cpu_steps or cfg["steps"]
+    steps = steps or args.cpu_steps or cfg["steps"]
     V = 7 if cfg["k"] == 1 else 343
     dc = DecoderConfig(vocab_size=V, rope_theta=1e6)
     tm = TorchCPUModel(OracleConfig(vocab_size=V, rope_theta=1e6), make_weights(dc, seed=0, init="normal"),
@@ -148,17 +148,20 @@ def cpu_baseline(args, cfg):
     bases = int(tm.tok.n_bases[out].sum())
     return {"value": bases / dt, "unit": "bases/s", "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"{B} chunks x {PLEN} frames, prefill + {steps} greedy steps, PyTorch CPU fp32 restatement "
-                      f"of the reference path ({dt:.1f} s)"}
+                      f"of the reference path ({dt:.1f} s)", "seconds": dt}
 
 
 def run_reference_arm(args, cfg, rank):
     if rank != 0:
         return
+    for _ in range(args.warmup):  # untimed warm-up steps on a short sample (the same code path, 16 decode steps)
+        cpu_baseline(args, cfg, steps=16)
     res = [cpu_baseline(args, cfg) for _ in range(max(1, args.steps))]
     vals = [r["value"] for r in res]
     v = statistics.median(vals)
+    ms = statistics.median(r.pop("seconds") for r in res) * 1e3
     line = {"metric": "decoded bases/s", "value": v, "unit": "bases/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
             "config": {"workload": cfg["name"], "sample": res[0]["sample"]},
             "cpu_baseline": dict(res[0], value=v),
@@ -371,6 +374,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args, cfg)
+        cpu.pop("seconds")
 
     if rank == 0:
         line = {"metric": "decoded bases/s", "value": value, "unit": "bases/s", "n_gpus": world, "steps": args.steps,
