@@ -43,6 +43,13 @@ int vk_read_device_errors(uint32_t* bits, int clear);
 /* Enables (1) or disables (0) programmatic dependent launch between consecutive kernels.  Default 1. */
 int vk_set_pdl(int enable);
 
+/* Test hook of the failure path (no reference counterpart; the reference's inference path has no device-side
+ * waits).  Launches one CTA whose thread waits on an mbarrier that nothing arrives on, bounded by limit_ns
+ * (0 < limit_ns <= 1e9): the wait runs out, the kernel sets VK_DEVERR_WAIT_FULL in the device error word,
+ * stores the nanoseconds it waited in *waited_ns (device, u64, may be NULL) and returns, leaving the context
+ * usable.  No copy is in flight while it waits. */
+int vk_test_bounded_wait(uint64_t limit_ns, unsigned long long* waited_ns, void* stream);
+
 /* ---- fused row ops: viktor/triton_ops.py ------------------------------------------------------------------ */
 
 /* viktor/triton_ops.py:34-40 add_rmsnorm.  x [n, d] bf16 (updated in place by += delta when delta != NULL),
@@ -145,7 +152,9 @@ int vk_decode_attention_i8(const void* q, const void* k_cache, const void* v_cac
  * without a CUDA allocator of their own, code that must not allocate once serving has started.
  * Limits: nq <= 256 queries and S <= 4096 cache positions; larger requests return VK_ERR_ARG with a message on
  * stderr.  The array (8.25 MiB) lives on every GPU that loads the library until the process exits.  The first
- * call on a device looks up the array's device address; make that first call before any stream capture.
+ * call on a device looks up the array's device address and keeps it for the life of the process; make that first
+ * call before any stream capture, and do not use this entry point on a device after cudaDeviceReset (the kept
+ * address would no longer be mapped).  `stream` must belong to the current device (VK_ERR_ARG otherwise).
  * Every call clears the per-query tickets it uses and then shares the device's array with all other calls on
  * that device: calls whose executions overlap on the same GPU (for example on concurrent streams) corrupt each
  * other's results — issue them in order on one stream per device.  Each device has its own array. */

@@ -40,6 +40,9 @@ def test_argument_errors_are_status_codes():
     assert lib.vk_add_rmsnorm(None, None, None, None, 4, 512, 1e-6, None) == _lib.VK_ERR_ARG
     assert lib.vk_add_rmsnorm(None, None, None, None, 0, 512, 1e-6, None) == _lib.VK_OK
     assert lib.vk_linear(None, None, None, 4, 64, 512, 0, 0, None) == _lib.VK_ERR_ARG
+    # the failure-path probe: its wait limit must lie in (0, 1 s]
+    assert lib.vk_test_bounded_wait(0, None, None) == _lib.VK_ERR_ARG
+    assert lib.vk_test_bounded_wait(2_000_000_000, None, None) == _lib.VK_ERR_ARG
     assert lib.vk_decode_attention(None, None, None, None, None, 4, 0, 4, 100, 12800, 128, None, 0,
                                    None) == _lib.VK_ERR_ARG
     # sampling needs the noise buffer and a positive, finite temperature

@@ -243,3 +243,25 @@ def test_pinned_host_frames_equal_device_frames():
     pinned = eng.generate(frames.pin_memory(), lens, 12).clone()
     pageable = eng.generate(frames, lens, 12).clone()
     assert torch.equal(pinned, ref) and torch.equal(pageable, ref)
+
+
+def test_engine_from_a_model_built_from_the_reference_checkpoint_map():
+    """DecodeEngine built from a model assembled only from the reference's state-dict names and shapes
+    (tests/golden/reference_state_dict.json, recorded from the stock viktor.Basecaller) decodes exactly as one
+    built from this package's Basecaller with the same weights."""
+    from test_checkpoint import MAP, reference_like_model
+    from viktor_b200 import Basecaller, DecodeEngine, DecoderConfig
+    from viktor_b200.synthetic import make_frames, make_weights
+    for key, k in (("k1", 1), ("k4", 4)):
+        cfg = DecoderConfig(vocab_size=MAP[key]["vocab_size"], rope_theta=1e6)
+        weights = make_weights(cfg, seed=31 + k, init="torch")
+        lens = [64, 200, 1, 130]
+        frames = torch.from_numpy(make_frames(lens, seed=33))
+        outs = []
+        for model in (reference_like_model(MAP[key]["params"], k, weights).cuda(),
+                      Basecaller.from_weights(weights, k=k, cfg=cfg)):
+            model.decoder.cfg = cfg
+            eng = DecodeEngine(model, len(lens), 16, max(lens), max_homopolymer=None, device="cuda")
+            eng.bias[2] = float("-inf")
+            outs.append(eng.generate(frames, lens, 16).clone())
+        assert torch.equal(outs[0], outs[1])

@@ -21,9 +21,11 @@ def test_shard_merge_round_trip(mode, n, world):
     assert np.array_equal(np.sort(seen), np.arange(n))
 
 
-def fake_decode(rank, world, indices, fail_rank):
+def fake_decode(rank, world, indices, fail_rank, how="raise"):
     """Stands in for a per-GPU engine: 'tokens' are a function of the chunk index only."""
     if rank == fail_rank:
+        if how == "exit0":
+            os._exit(0)  # leaves without a result and without an error code
         raise RuntimeError("simulated device failure")
     return np.stack([np.arange(5) + 100 * i for i in indices]) if len(indices) else np.zeros((0, 5), int)
 
@@ -39,6 +41,17 @@ def test_run_sharded_reports_the_failing_shard():
     with pytest.raises(ShardError) as e:
         run_sharded(fake_decode, 8, 2, args=(1,), timeout=120)
     assert e.value.rank == 1
+
+
+def test_run_sharded_reports_a_worker_that_exits_without_result():
+    """A worker that ends with exit code 0 but never answered fails its shard within seconds (not at the
+    call's timeout)."""
+    import time
+    t0 = time.monotonic()
+    with pytest.raises(ShardError) as e:
+        run_sharded(fake_decode, 8, 2, args=(0, "exit0"), timeout=600)
+    assert e.value.rank == 0
+    assert time.monotonic() - t0 < 60
 
 
 def _free_port():

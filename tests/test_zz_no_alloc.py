@@ -4,8 +4,9 @@ Some hosts of this library cannot allocate device memory for a kernel's scratch 
 APIs that pass a kernel only its inputs and outputs, FFI callers without a CUDA allocator, serving code that
 must not allocate after start-up).  vk_decode_attention_noalloc serves them from a fixed array inside the
 library.  This test calls it through the C ABI twice in a row (the array keeps the previous call's contents)
-and compares it with vk_decode_attention using a freshly allocated workspace, at the tolerance of the other
-decode-attention tests (0.01 max-abs; the two share one kernel, so the outputs are expected to be identical).
+and compares it with vk_decode_attention using a freshly allocated workspace, and both with an fp32 attention
+computed by PyTorch, at the tolerance of the other decode-attention tests (0.01 max-abs; the two entry points
+share one kernel, so their outputs are expected to be identical).
 It is collected last so that a failure here never hides the rest of the suite, and it needs no state from
 other tests.
 """
@@ -41,6 +42,16 @@ def _run(name, q, k, v, lens, ws=None):
     return out
 
 
+def _fp32_attention(q, k, v, lens):
+    """softmax(q . K[:L]^T / 8) . V[:L] per query in fp32 (GQA: query head h reads KV head h // 4)."""
+    B, S = k.shape[0], k.shape[1]
+    kk = k.float().permute(0, 2, 1, 3).repeat_interleave(4, 1)  # [B, 8, S, 64]
+    vv = v.float().permute(0, 2, 1, 3).repeat_interleave(4, 1)
+    mask = (torch.arange(S, device=k.device)[None, :] < lens[:, None].long())[:, None, None, :]
+    o = torch.nn.functional.scaled_dot_product_attention(q.float()[:, :, None, :], kk, vv, attn_mask=mask)
+    return o[:, :, 0, :]
+
+
 def test_noalloc_matches_workspace_entry_point_twice():
     from viktor_b200._lib import check_device_errors, load
     lib = load()
@@ -52,6 +63,9 @@ def test_noalloc_matches_workspace_entry_point_twice():
         torch.cuda.synchronize()
         check_device_errors()
         assert (got.float() - ref.float()).abs().max().item() < 0.01
+        exact = _fp32_attention(q, k, v, lens)
+        assert (got.float() - exact).abs().max().item() < 0.01
+        assert (ref.float() - exact).abs().max().item() < 0.01
 
 
 def test_noalloc_rejects_sizes_beyond_its_array():

@@ -180,6 +180,24 @@ static gemm::EpiArgs epi_zero() {
   return e;
 }
 
+// Failure-path probe: one CTA whose first thread waits on an mbarrier that nothing arrives on (no copy in flight,
+// no other thread involved).  The bounded wait gives up after limit_ns, the thread records ERR_WAIT_FULL exactly
+// as a pipeline wait that ran out does, writes how long it waited and the kernel returns normally.
+__global__ void bounded_wait_probe_kernel(uint64_t limit_ns, unsigned long long* waited_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = globaltimer();
+    const bool done = mbar_wait_for(&bar, 0, limit_ns);
+    if (!done) raise_error(ERR_WAIT_FULL);
+    if (waited_ns) *waited_ns = globaltimer() - t0;
+  }
+}
+
 
 }  // namespace vk
 
@@ -202,6 +220,12 @@ int vk_read_device_errors(uint32_t* bits, int clear) {
 int vk_set_pdl(int enable) {
   vk::g_pdl = enable ? 1 : 0;
   return VK_OK;
+}
+
+int vk_test_bounded_wait(uint64_t limit_ns, unsigned long long* waited_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > vk::kWaitLimitNs) return VK_ERR_ARG;
+  bounded_wait_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns, waited_ns);
+  return cudaGetLastError() == cudaSuccess ? VK_OK : VK_ERR_CUDA;
 }
 
 int vk_add_rmsnorm(void* x, const void* delta, const void* w, void* h, int64_t n, int d, float eps, void* stream) {
@@ -638,6 +662,14 @@ int vk_decode_attention_noalloc(const void* q, const void* k_cache, const void* 
   static void* scratch[64] = {nullptr};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VK_ERR_CUDA;
+  // the array used is the current device's: a stream of another device would run against memory it cannot see
+  int stream_dev = dev;
+  if (cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &stream_dev) != cudaSuccess) return VK_ERR_CUDA;
+  if (stream_dev != dev) {
+    fprintf(stderr, "viktor_b200: vk_decode_attention_noalloc: the stream belongs to device %d, the current device "
+                    "is %d\n", stream_dev, dev);
+    return VK_ERR_ARG;
+  }
   if (!scratch[dev]) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, vk::g_noalloc_attn_scratch) != cudaSuccess || !p) {

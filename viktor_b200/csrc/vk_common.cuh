@@ -76,18 +76,19 @@ VK_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity to complete.  Returns false if it ran out.  The timer is
-// read once per 64 polls so that the common case costs only the mbarrier probes.
-VK_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Bounded wait for the phase with the given parity to complete.  Returns false if it ran out (after limit_ns of
+// %globaltimer).  The timer is read once per 64 polls so that the common case costs only the mbarrier probes.
+VK_DEV bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    if (globaltimer() - t0 > limit_ns) return false;
   }
 }
+VK_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) { return mbar_wait_for(bar, parity, kWaitLimitNs); }
 
 // ---- TMA bulk-tensor loads into this CTA's own shared memory ------------------------------------------------
 VK_DEV void tma_prefetch_desc(const CUtensorMap* map) {

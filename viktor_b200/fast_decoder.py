@@ -30,21 +30,61 @@ def _p(t):
     return None if t is None else t.data_ptr()
 
 
+def expected_shapes(cfg, d_enc: int = 512) -> dict:
+    """The checkpoint entries the engine reads, name -> shape: the ``projector.*`` and ``decoder.*`` keys of the
+    reference model's state dict (viktor/model.py:35, viktor/decoder.py:54-134)."""
+    d, f, hd = cfg.d_model, cfg.ffn_dim, cfg.head_dim
+    qkv = (cfg.n_heads + 2 * cfg.n_kv_heads) * hd
+    shapes = {"projector.0.weight": (d, d_enc), "projector.0.bias": (d,), "projector.2.weight": (d, d),
+              "projector.2.bias": (d,), "decoder.embed.weight": (cfg.vocab_size, d), "decoder.norm.weight": (d,),
+              "decoder.lm_head.weight": (cfg.vocab_size, d)}
+    for i in range(cfg.n_layers):
+        p = f"decoder.layers.{i}."
+        shapes.update({p + "attn_norm.weight": (d,), p + "attn.qkv_proj.weight": (qkv, d),
+                       p + "attn.q_norm.weight": (hd,), p + "attn.k_norm.weight": (hd,),
+                       p + "attn.o_proj.weight": (d, cfg.n_heads * hd), p + "mlp_norm.weight": (d,),
+                       p + "gate_up.weight": (2 * f, d), p + "down.weight": (d, f)})
+    return shapes
+
+
+def check_state_dict(shapes: dict, cfg, d_enc: int = 512):
+    """Raises ValueError unless ``shapes`` (name -> shape of the model's projector/decoder entries) has exactly
+    the entries expected_shapes() lists, with those shapes.  Host only (no tensors are touched)."""
+    want = expected_shapes(cfg, d_enc)
+    missing = sorted(set(want) - set(shapes))
+    extra = sorted(set(shapes) - set(want))
+    bad = sorted(n for n in want if n in shapes and tuple(shapes[n]) != want[n])
+    if missing or extra or bad:
+        raise ValueError(f"checkpoint does not match the decoder: missing {missing[:4]}, unexpected {extra[:4]}, "
+                         f"shape mismatch {[(n, tuple(shapes[n]), want[n]) for n in bad[:4]]}")
+
+
+def model_state(model) -> dict:
+    """The projector and decoder entries of a Basecaller-like model (this package's or the reference's
+    viktor.model.Basecaller: anything with ``projector`` and ``decoder`` modules), keyed as in its state dict."""
+    sd = {f"projector.{n}": t for n, t in model.projector.state_dict().items()}
+    sd.update({f"decoder.{n}": t for n, t in model.decoder.state_dict().items()})
+    return sd
+
+
 class DeviceWeights:
-    """bf16 device copies of the projector + decoder weights, in the layouts the kernels read.  The attention
-    norm of each layer is folded into its qkv weight, the MLP norm into gate_up and the final norm into lm_head
-    (columns scaled by the norm weight, rounded once to bf16)."""
+    """bf16 device copies of the projector + decoder weights, in the layouts the kernels read, taken from the
+    model's state-dict entries by their reference names.  The attention norm of each layer is folded into its
+    qkv weight, the MLP norm into gate_up and the final norm into lm_head (columns scaled by the norm weight,
+    rounded once to bf16)."""
 
     def __init__(self, model, device):
-        dec = model.decoder
-        cfg = dec.cfg
+        cfg = model.decoder.cfg
         if (cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim) != (512, 8, 2, 64):
             raise NotImplementedError("the kernels are built for d_model 512, 8 query / 2 KV heads, head_dim 64")
         if cfg.ffn_dim % 128:
             raise NotImplementedError("ffn_dim must be a multiple of 128")
+        sd = model_state(model)
+        d_enc = sd["projector.0.weight"].shape[1] if "projector.0.weight" in sd else -1
+        check_state_dict({n: tuple(t.shape) for n, t in sd.items()}, cfg, d_enc)
 
-        def w(t):
-            return t.detach().to(device=device, dtype=_BF16).contiguous()
+        def w(name):
+            return sd[name].detach().to(device=device, dtype=_BF16).contiguous()
 
         def fold(weight, norm):
             out = torch.empty_like(weight)
@@ -54,26 +94,26 @@ class DeviceWeights:
 
         self.cfg = cfg
         self.eps = float(cfg.norm_eps)
-        self.embed = w(dec.embed.weight)
+        self.embed = w("decoder.embed.weight")
         self.vocab = cfg.vocab_size
         # lm_head rows padded to a multiple of 16 (tensor-core N granularity); padded logits are never read
         vpad = -(-cfg.vocab_size // 16) * 16
         head = torch.zeros(vpad, cfg.d_model, dtype=_BF16, device=device)
-        head[:cfg.vocab_size] = w(dec.lm_head.weight)
-        self.norm = w(dec.norm.weight)
+        head[:cfg.vocab_size] = w("decoder.lm_head.weight")
+        self.norm = w("decoder.norm.weight")
         self.lm_head, self.vpad = fold(head, self.norm), vpad
         self.layers = []
-        for blk in dec.layers:
-            a = blk.attn
-            self.layers.append(dict(qkv=fold(w(a.qkv_proj.weight), w(blk.attn_norm.weight)),
-                                    q_norm=w(a.q_norm.weight), k_norm=w(a.k_norm.weight), o=w(a.o_proj.weight),
-                                    gate_up=fold(w(blk.gate_up.weight), w(blk.mlp_norm.weight)),
-                                    down=w(blk.down.weight)))
+        for i in range(cfg.n_layers):
+            p = f"decoder.layers.{i}."
+            self.layers.append(dict(qkv=fold(w(p + "attn.qkv_proj.weight"), w(p + "attn_norm.weight")),
+                                    q_norm=w(p + "attn.q_norm.weight"), k_norm=w(p + "attn.k_norm.weight"),
+                                    o=w(p + "attn.o_proj.weight"),
+                                    gate_up=fold(w(p + "gate_up.weight"), w(p + "mlp_norm.weight")),
+                                    down=w(p + "down.weight")))
         cos, sin = rope_tables(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta)
         self.cos, self.sin = cos.to(device).contiguous(), sin.to(device).contiguous()
-        proj = model.projector
-        self.proj = (w(proj[0].weight), w(proj[0].bias), w(proj[2].weight), w(proj[2].bias))
-        self.d_enc = proj[0].weight.shape[1]
+        self.proj = (w("projector.0.weight"), w("projector.0.bias"), w("projector.2.weight"), w("projector.2.bias"))
+        self.d_enc = d_enc
         if self.d_enc % 64:
             raise NotImplementedError("encoder width must be a multiple of 64")
 

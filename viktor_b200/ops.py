@@ -128,7 +128,9 @@ def decode_attention(q, k, v, lengths, block=64, workspace=None, row0=0):
         raise NotImplementedError("decode attention kernels are built for 8 query / 2 KV heads")
     S = k.shape[1]
     if workspace is None:
-        key = (q.device, B, S)
+        # one implicit workspace per (device, shape, stream): calls on the same stream run one after another;
+        # calls on different streams get different workspaces, so they never share split-K tickets or partials
+        key = (q.device, B, S, _stream(q))
         workspace = _WS.get(key)
         if workspace is None:
             workspace = _WS[key] = decode_attention_workspace(B, S, q.device)

@@ -80,24 +80,40 @@ def run_sharded(worker, n_items: int, world: int, args=(), mode: str = "strided"
         procs.append(p)
     out = [None] * world
     got = 0
+
+    def take(item):
+        nonlocal got
+        rank, ok, payload = item
+        if not ok:
+            raise ShardError(rank, payload.strip().splitlines()[-1] if payload else "error")
+        if out[rank] is None:
+            out[rank] = (payload,)
+            got += 1
+
     try:
         import time
         deadline = time.monotonic() + timeout
         while got < world:
             try:
-                rank, ok, payload = results.get(timeout=0.5)
+                take(results.get(timeout=0.5))
             except queue.Empty:
-                for r, p in enumerate(procs):
-                    if out[r] is None and not p.is_alive() and p.exitcode not in (0, None):
-                        raise ShardError(r, f"process exited with code {p.exitcode}")
+                dead = [r for r, p in enumerate(procs) if out[r] is None and not p.is_alive()]
+                if dead:
+                    # a worker that finished without a result in hand: its result may still be in the queue's pipe
+                    # (the feeder flushes it on exit), so drain for a moment before declaring the shard failed
+                    drain_until = time.monotonic() + 2.0
+                    while got < world and time.monotonic() < drain_until:
+                        try:
+                            take(results.get(timeout=0.2))
+                        except queue.Empty:
+                            pass
+                    for r in dead:
+                        if out[r] is None:
+                            raise ShardError(r, f"process exited with code {procs[r].exitcode} without a result")
                 if time.monotonic() > deadline:
                     missing = [r for r in range(world) if out[r] is None]
                     raise ShardError(missing[0], f"no result after {timeout:.0f} s")
                 continue
-            if not ok:
-                raise ShardError(rank, payload.strip().splitlines()[-1] if payload else "error")
-            out[rank] = (payload,)
-            got += 1
     finally:
         for p in procs:
             if p.is_alive() and any(o is None for o in out):
