@@ -231,13 +231,18 @@ int vk_copy_rows(const void* src, const int64_t* src_idx, int64_t src_rows, void
  * is the lm_head with the final RMSNorm weight folded in (logits = rsqrt(mean(x^2) + eps) * x . head_w^T, fp32,
  * as the fp32-output linear of viktor/engine.py:95-96); V <= 512.  The remaining arguments are those of
  * vk_sample_update; noise = NULL selects greedily (vk_greedy_update).  x / ssq may alias x_final / ssq_final
- * (each row is read before it is overwritten with the next token's embedding). */
+ * (each row is read before it is overwritten with the next token's embedding).
+ * limit [B] i64 or NULL: per-row output cap; the token of output column >= limit[b] becomes EOS (a stand-in for
+ * a model that ends its read there; the reference's grammar has no such rule, NULL keeps it exact).
+ * shrink_done != 0: a row whose new token is EOS or PAD gets seqlens = 1 instead of pos + 1.  That row's next
+ * output is PAD whatever the step computes (viktor/engine.py:88), so its attention then reads one cached
+ * position instead of its whole row; no output token changes. */
 int vk_head_select(const void* x_final, const float* ssq_final, float eps, const void* head_w, const float* bias,
                    const uint8_t* is_tail, const uint8_t* is_homo, int homo_stop, int64_t* tok, int64_t* run,
                    int64_t* pos, const int64_t* plen, const int64_t* rope_off, int64_t* out, int64_t out_stride,
                    int64_t out_cols, int32_t* pos32, int32_t* seqlens, int32_t* rpos32, int B, int V, int eos, int pad,
                    const void* emb, void* x, float* ssq, const float* noise, int64_t ld_noise, float temperature,
-                   void* stream);
+                   const int64_t* limit, int shrink_done, void* stream);
 
 /* The packed prefill layout of viktor/engine.py:145-159, built on the device from the prefix lengths of one
  * sub-batch (lens [n] i32 on the device, 1 <= n <= 4096; total = sum(lens) + n, known to the caller).

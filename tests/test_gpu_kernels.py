@@ -374,7 +374,7 @@ def test_head_select_equals_lm_head_then_greedy():
              2, 0, p(emb), p(s1["x"]), p(s1["ssq"]), st)
         call("vk_head_select", p(x), p(ssq), 1e-6, p(w), p(bias), p(tail), p(homo), 0, p(s2["tok"]), p(s2["run"]),
              p(s2["pos"]), p(s2["plen"]), p(s2["roff"]), p(s2["out"]), 8, 8, p(s2["p32"]), p(s2["sl"]), p(s2["rp"]), B, V,
-             2, 0, p(emb), p(s2["x"]), p(s2["ssq"]), None, 0, 1.0, st)
+             2, 0, p(emb), p(s2["x"]), p(s2["ssq"]), None, 0, 1.0, None, 0, st)
         torch.cuda.synchronize()
         top2 = (logits + bias).topk(2, 1).values
         clear = (top2[:, 0] - top2[:, 1]) > 1e-3
@@ -383,3 +383,54 @@ def test_head_select_equals_lm_head_then_greedy():
         for key in ("pos", "p32", "sl", "rp"):
             assert torch.equal(s1[key], s2[key])
         assert torch.equal(s1["x"][clear], s2["x"][clear])
+
+
+def test_head_select_output_cap_and_finished_rows():
+    """The per-row output cap (limit) ends a row with EOS at column limit[b]; with shrink_done, rows whose new
+    token is EOS or PAD get seqlens 1 (their next output is PAD regardless), the others pos + 1; tokens, pos and
+    the output row are what they are without shrink_done."""
+    from viktor_b200._lib import call
+    from viktor_b200.config import KmerTokenizer
+    from viktor_b200.engine import _masks
+    tk = KmerTokenizer(1)
+    V, B = tk.vocab_size, 8
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(B, 512, generator=g, device=DEV).to(BF)
+    xf = x.float()
+    ssq = torch.stack([(xf[:, 64 * i:64 * (i + 1)] ** 2).sum(1) for i in range(8)], 1).contiguous()
+    w = (torch.randn(V, 512, generator=g, device=DEV) * 0.3).to(BF)
+    bias = torch.zeros(V, device=DEV)
+    bias[:3] = float("-inf")  # PAD, BOS, EOS never chosen by the argmax
+    tail, homo = _masks(tk, torch.device(DEV))
+    emb = torch.randn(V, 512, generator=g, device=DEV).to(BF)
+    st = torch.cuda.current_stream().cuda_stream
+    # rows at output columns 0..7 (pos - plen); row 6 had emitted EOS, row 7 PAD
+    plen = torch.full((B,), 100, dtype=torch.long, device=DEV)
+    col = torch.arange(8, dtype=torch.long, device=DEV)
+    limit = torch.tensor([0, 5, 2, 9, 4, 6, 1, 1], dtype=torch.long, device=DEV)
+    prev = torch.tensor([1, 3, 4, 5, 6, 3, 2, 0], dtype=torch.long, device=DEV)
+    outs = {}
+    for shrink in (0, 1):
+        s = dict(tok=prev.clone(), run=torch.zeros(B, dtype=torch.long, device=DEV), pos=plen + col, plen=plen,
+                 roff=torch.zeros(B, dtype=torch.long, device=DEV),
+                 out=torch.full((B, 8), -1, dtype=torch.long, device=DEV),
+                 p32=torch.zeros(B, dtype=torch.int32, device=DEV), sl=torch.zeros(B, dtype=torch.int32, device=DEV),
+                 rp=torch.zeros(B, dtype=torch.int32, device=DEV), x=torch.empty(B, 512, dtype=BF, device=DEV),
+                 ssq=torch.empty(B, 8, device=DEV))
+        p = lambda t: t.data_ptr()
+        call("vk_head_select", p(x), p(ssq), 1e-6, p(w), p(bias), p(tail), p(homo), 0, p(s["tok"]), p(s["run"]),
+             p(s["pos"]), p(s["plen"]), p(s["roff"]), p(s["out"]), 8, 8, p(s["p32"]), p(s["sl"]), p(s["rp"]), B, V,
+             2, 0, p(emb), p(s["x"]), p(s["ssq"]), None, 0, 1.0, p(limit), shrink, st)
+        torch.cuda.synchronize()
+        outs[shrink] = s
+    a, b = outs[0], outs[1]
+    tok = b["tok"].cpu().tolist()
+    # col >= limit -> EOS (rows 0, 2, 4, 5); below the cap: a base (rows 1, 3); after EOS / PAD: PAD (rows 6, 7)
+    assert [tok[i] for i in (0, 2, 4, 5)] == [2, 2, 2, 2]
+    assert tok[1] >= 3 and tok[3] >= 3
+    assert tok[6] == 0 and tok[7] == 0
+    for key in ("tok", "pos", "p32", "out", "rp"):
+        assert torch.equal(a[key], b[key]), key
+    assert torch.equal(a["sl"], (plen + col + 2).int())
+    ended = torch.tensor([t in (0, 2) for t in tok], device=DEV)
+    assert torch.equal(b["sl"], torch.where(ended, torch.ones_like(a["sl"]), a["sl"]))

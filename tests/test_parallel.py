@@ -85,3 +85,36 @@ def test_reduce_bench_on_gloo_world_of_two():
     for r in range(2):
         e, d, pf, b = res[r]
         assert (e, d, pf, b) == (2.0, 1.0, 0.1, 3000)
+
+
+def _gloo_gather_rank(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    from viktor_b200.parallel import gather_tokens
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        tok = torch.arange(12, dtype=torch.int64).reshape(3, 4) + 1000 * rank
+        tok[0, 0] = 342  # the largest 4-mer token id survives the int16 transport
+        got = gather_tokens(tok)
+        q.put((rank, None if got is None else got.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_tokens_on_gloo_world_of_two():
+    """The final token gather: rank 0 receives every rank's [rows, cols] tokens in rank order, others None."""
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_gather_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=30)
+    assert res[1] is None
+    want = np.concatenate([np.arange(12).reshape(3, 4) + 1000 * r for r in range(2)])
+    want[0, 0] = want[3, 0] = 342
+    assert res[0].dtype == np.int16 and np.array_equal(res[0], want)

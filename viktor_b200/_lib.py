@@ -31,7 +31,7 @@ _SIGS = {
     "vk_greedy_update": (i32, [p, i64, p, p, p, i32, p, p, p, p, p, p, i64, i64, p, p, p, i32, i32, i32, i32, p, p,
                                p, p]),
     "vk_head_select": (i32, [p, p, f32, p, p, p, p, i32, p, p, p, p, p, p, i64, i64, p, p, p, i32, i32, i32, i32, p, p, p,
-                             p, i64, f32, p]),
+                             p, i64, f32, p, i32, p]),
     "vk_prefill_plan": (i32, [p, i32, i32, i32, i64, p, p, p, p, p, p, p, p]),
     "vk_sample_update": (i32, [p, i64, p, p, p, i32, p, p, p, p, p, p, i64, i64, p, p, p, i32, i32, i32, i32, p, p,
                                p, p, i64, f32, p]),

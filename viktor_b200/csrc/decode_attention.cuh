@@ -566,12 +566,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     // While the previous kernel finishes: the first tiles of this split into L2.  Cache rows older than this
     // step's newest position were written by earlier grids; the prefetch only warms L2 (the loads after the
     // wait read whatever L2 then holds).
+    // The row's length as last written (this step's, or the previous step's if the kernel that advances it is
+    // still running: at most one position short) only bounds the prefetch, so tiles past the row's end (splits
+    // past it, rows that have ended) are not pulled from HBM.
     const int p0 = split * a.chunk, crow = a.row0 + b;
+    const int len_hint = *reinterpret_cast<const volatile int32_t*>(a.lengths + b);
     for (int t = 0; t < kStages; ++t)
-      for (int h = 0; h < 2; ++h) {
-        tma_prefetch_l2_4d(&tmK, 0, h, p0 + t * kTile, crow);
-        tma_prefetch_l2_4d(&tmV, 0, h, p0 + t * kTile, crow);
-      }
+      if (p0 + t * kTile <= len_hint)
+        for (int h = 0; h < 2; ++h) {
+          tma_prefetch_l2_4d(&tmK, 0, h, p0 + t * kTile, crow);
+          tma_prefetch_l2_4d(&tmV, 0, h, p0 + t * kTile, crow);
+        }
   }
   pdl_wait();  // q, lengths and the newest cache row come from the previous kernel
   if (b >= a.nq) return;

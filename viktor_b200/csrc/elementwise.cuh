@@ -200,6 +200,12 @@ struct GreedyArgs {
   const float* head_ssq;
   const __nv_bfloat16* head_w;
   float head_eps;
+  // optional per-row output cap: row b's token in output column limit[b] (and any later one) is EOS, so the row
+  // emits at most limit[b] tokens before it ends (nullptr = no cap)
+  const int64_t* limit;
+  // 1: a row whose next input token is EOS or PAD gets seqlens = 1 for the next step.  Its next output is PAD
+  // whatever that step computes, so its attention reads one position instead of its whole cache row.
+  int shrink_done;
 };
 constexpr int kHeadMaxV = 512;  // vocabulary of the fused head (the 4-mer vocabulary has 343 tokens)
 
@@ -290,8 +296,9 @@ __global__ void __launch_bounds__(128) greedy_kernel(GreedyArgs a) {
       a.run[b] = run;
       if (run + 1 >= a.homo_stop) nxt = a.eos;
     }
-    if (prev == a.eos || prev == a.pad) nxt = a.pad;
     const int64_t col = p - pl;
+    if (a.limit && col >= a.limit[b]) nxt = a.eos;  // the row's output cap: end it here
+    if (prev == a.eos || prev == a.pad) nxt = a.pad;
     if (col >= 0 && col < a.out_cols)
       a.out[static_cast<int64_t>(b) * a.out_stride + col] = nxt;
     else
@@ -300,7 +307,7 @@ __global__ void __launch_bounds__(128) greedy_kernel(GreedyArgs a) {
     p += 1;
     a.pos[b] = p;
     a.pos32[b] = static_cast<int32_t>(p);
-    a.seqlens[b] = static_cast<int32_t>(p + 1);
+    a.seqlens[b] = (a.shrink_done && (nxt == a.eos || nxt == a.pad)) ? 1 : static_cast<int32_t>(p + 1);
     a.rpos32[b] = static_cast<int32_t>(p + roff);
     chosen = nxt;
   }

@@ -440,7 +440,7 @@ int vk_head_select(const void* x_final, const float* ssq_final, float eps, const
                    int64_t* pos, const int64_t* plen, const int64_t* rope_off, int64_t* out, int64_t out_stride,
                    int64_t out_cols, int32_t* pos32, int32_t* seqlens, int32_t* rpos32, int B, int V, int eos, int pad,
                    const void* emb, void* x, float* ssq, const float* noise, int64_t ld_noise, float temperature,
-                   void* stream) {
+                   const int64_t* limit, int shrink_done, void* stream) {
   if (B == 0) return VK_OK;
   if (!x_final || !ssq_final || !head_w || V > ew::kHeadMaxV || !aligned16(x_final) || !aligned16(ssq_final) ||
       !aligned16(head_w) ||
@@ -454,6 +454,8 @@ int vk_head_select(const void* x_final, const float* ssq_final, float eps, const
   a.head_ssq = ssq_final;
   a.head_w = static_cast<const __nv_bfloat16*>(head_w);
   a.head_eps = eps;
+  a.limit = limit;
+  a.shrink_done = shrink_done ? 1 : 0;
   if (noise) {
     a.noise = noise;
     a.ld_noise = ld_noise;

@@ -116,6 +116,15 @@ class DecodeEngine:
         self.homo_stop = max_homopolymer // tk.k if max_homopolymer else 0
         self.run = torch.zeros(B, dtype=torch.long, device=dev)
         self.plen = torch.zeros(B, dtype=torch.long, device=dev)
+        # Per-row output cap (an extension; the reference has none): the token of output column max_tokens[b]
+        # is EOS, so row b emits at most max_tokens[b] tokens before it ends.  The default, max_new_tokens, never
+        # triggers.  A benchmark sets it to stand in for a trained model that ends each read at its own length.
+        self.max_tokens = torch.full((B,), max_new_tokens, dtype=torch.long, device=dev)
+        # Rows that have ended decode at the cost of one cached position per layer: after EOS every output is PAD
+        # whatever the step computes (viktor/engine.py:88), so the selection kernel gives such a row seqlens 1
+        # and its attention skips the rest of its cache row.  Output tokens are unchanged.  (Not with the int8
+        # prefix mode, whose attention needs every row's length past its int8 prefix.)
+        self.skip_finished = not kv_int8
 
         # decode-step activations: residual x and the block sums of squares of its rows (folded RMSNorms)
         self.x = torch.zeros(B, d, dtype=_BF16, device=dev)
@@ -213,7 +222,7 @@ class DecodeEngine:
              _p(self.is_homo), self.homo_stop, _p(self.tok[r]), _p(self.run[r]), _p(self.pos[r]), _p(self.plen[r]),
              _p(self.rope_off[r]), _p(self.out[r]), self.out.stride(0), self.out.shape[1], _p(self.pos32[r]),
              _p(self.seqlens[r]), _p(self.rpos32[r]), hi - lo, w.vocab, EOS, PAD, _p(w.embed), _p(self.x[r]),
-             _p(self.ssq[r]), *noise, st)
+             _p(self.ssq[r]), *noise, _p(self.max_tokens[r]), 1 if self.skip_finished else 0, st)
 
     @torch.no_grad()
     def _capture(self):

@@ -10,6 +10,8 @@ at the end (the pattern of scripts/evaluate.py:127-138, and of `sharded_calls` i
   collect the results in rank order.  A worker that raises, exits or does not answer makes the call raise
   ``ShardError`` naming the rank (the other workers are stopped), so a caller never gets a silently partial
   result.
+* ``gather_tokens``: the final gather of every rank's token array onto one host (rank 0), over the process
+  group (NCCL over NVLink between GPUs), then one copy into pinned host memory.
 * ``reduce_bench``: the timing reduction used by ``bench.py`` under ``torch.distributed`` (max of the elapsed
   times, sum of the bases), written against any backend (NCCL on GPUs, gloo on CPU in the tests).
 """
@@ -120,6 +122,31 @@ def run_sharded(worker, n_items: int, world: int, args=(), mode: str = "strided"
                 p.terminate()
             p.join(timeout=5)
     return [o[0] for o in out]
+
+
+def gather_tokens(tokens, dst: int = 0, host_out=None):
+    """The final host gather of a data-parallel decode under ``torch.distributed``: every rank passes its token
+    array ``tokens`` [rows, cols] (the same shape on every rank, on the rank's device for NCCL or on the CPU for
+    gloo); rank ``dst`` gets the ranks' arrays concatenated in rank order as one CPU int16 tensor [world * rows,
+    cols] (token ids < 32768; the 4-mer vocabulary has 343), the other ranks get None.  Tokens cross NVLink as
+    int16 (a quarter of the engine's int64 buffer) and reach the host in one copy into pinned memory
+    (``host_out``, a pinned int16 tensor of the gathered shape, when given; else a new one)."""
+    import torch
+    import torch.distributed as dist
+    world, rank = dist.get_world_size(), dist.get_rank()
+    # int16 travels as its bytes: neither NCCL nor gloo has a 16-bit integer type, and a gather only moves bytes
+    t8 = tokens.to(torch.int16).contiguous().view(torch.uint8)
+    parts = [torch.empty_like(t8) for _ in range(world)] if rank == dst else None
+    dist.gather(t8, parts, dst=dst)
+    if rank != dst:
+        return None
+    allt = torch.cat(parts).view(torch.int16)
+    if allt.is_cuda:
+        host = host_out if host_out is not None else torch.empty(allt.shape, dtype=allt.dtype, pin_memory=True)
+        host.copy_(allt, non_blocking=True)
+        torch.cuda.current_stream(allt.device).synchronize()
+        return host
+    return allt
 
 
 def reduce_bench(elapsed_s: float, decode_s: float, prefill_s: float, bases: int, device=None):
