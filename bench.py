@@ -1,20 +1,28 @@
 """Benchmark of the Viktor decoder hot path on B200: decoded bases/s and microseconds per decode step.
 
-One bench step = one ``DecodeEngine.generate`` over a batch of chunks (packed prefill of the projected frames,
-then a fixed number of greedy CUDA-graph decode steps with EOS masked, so every step emits one token per
-chunk).  Default workload: 256 chunks x 2048 frames x 512 features ~ N(0, 1), 1100
-decode steps, single-base vocabulary (7), 8-layer d512 GQA 8/2 decoder with N(0, 0.02) random weights, bf16.
+One bench step = one ``DecodeEngine.generate`` per engine batch of this GPU's chunks (packed prefill of the
+projected frames, then greedy CUDA-graph decode steps with EOS masked, so every step emits one token per chunk
+until the chunk's own decode length).  Default workload: 256 chunks x 2048 frames x
+512 features ~ N(0, 1), 1100 decode steps, single-base vocabulary (7), 8-layer d512 GQA 8/2 decoder with
+N(0, 0.02) random weights, bf16.  Other BASELINE configs:
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4]
+    --config 3   512 chunks of U{128..2048 step 128} frames; chunk b decodes round(1100 x frames_b / 2048)
+                 tokens, then EOS and PAD (engine.max_tokens); decode(steps=None) stops when every chunk ended
+    --config 4   1024 chunks x 2048 frames, 4-mer vocabulary (343), 280 steps
+    --config 5   2048 chunks per GPU (config-2 lengths) in engine batches of 256 (--engine-batch), all ranks'
+                 tokens gathered to rank 0's host
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
 
 Multi-GPU: one process per GPU under torch.distributed.run; every rank runs its own engine on its own chunks
-(weak scaling, no collective on the data path); the barrier / max-over-ranks timing uses NCCL.
+(weak scaling, no collective on the data path); the barrier / max-over-ranks timing uses NCCL, and in the e2e
+region the token arrays of all ranks are gathered to rank 0 (NCCL) and copied to its host.
 
 Printed keys beyond the base contract:
   roofline      decode attention (the dominant kernel): algorithmic KV bytes per launch / measured launch time
   cpu_baseline  the reference path on the host cores (PyTorch CPU fp32 port) on a bounded sample, rank 0, N=1
-  e2e           the same metric through the public API from pinned host frames, tokens copied back each step
-  decode_us_per_step, prefill_ms_per_chunk, gpu_launches, clocks
+  e2e           the same metric through the public API from pinned host frames, tokens back on one host
+  decode_us_per_step (decode_ms_per_batch with per-chunk lengths), prefill_ms_per_chunk, gpu_launches, clocks
 """
 
 from __future__ import annotations
@@ -36,10 +44,13 @@ sys.path.insert(0, ROOT)
 CONFIGS = {
     2: dict(name="config2: 256 chunks x 2048 frames, 1100 greedy steps, vocab 7", B=256, frames="full", steps=1100,
             k=1),
-    3: dict(name="config3: 512 chunks x U{128..2048 step 128} frames, 1100 greedy steps, vocab 7", B=512,
-            frames="varlen", steps=1100, k=1),
+    3: dict(name="config3: 512 chunks x U{128..2048 step 128} frames, decode length 1100 x frames / 2048 (then "
+                 "EOS, PAD), vocab 7", B=512, frames="varlen", steps=1100, k=1, budget=True),
     4: dict(name="config4: 1024 chunks x 2048 frames, 280 greedy steps, 4-mer vocab 343", B=1024, frames="full",
             steps=280, k=4),
+    5: dict(name="config5: 2048 chunks per GPU x 2048 frames (config-2 lengths), 1100 greedy steps, vocab 7, "
+                 "tokens of every rank gathered to rank 0's host", B=2048, engine_batch=256, frames="full",
+            steps=1100, k=1),
 }
 PLEN = 2048
 HBM_FALLBACK_GBS = 6650.0
@@ -123,10 +134,20 @@ def make_lens(cfg, B, seed):
     return [PLEN] * B if cfg["frames"] == "full" else varlen_prefix_lengths(B, seed=seed)
 
 
+def make_budgets(cfg, lens):
+    """Per-chunk decode lengths of the workload: with cfg["budget"] (config 3), round(steps x frames / 2048)
+    tokens and then EOS; otherwise None (every chunk decodes the full number of steps, EOS masked)."""
+    if not cfg.get("budget"):
+        return None
+    return [int(round(cfg["steps"] * n / PLEN)) for n in lens]
+
+
 def cpu_baseline(args, cfg, steps=None):
     """The reference path on the host cores: a multithreaded PyTorch-CPU fp32 restatement (oracle/decoder_torch.py,
-    pinned to the reference's golden tokens) on a bounded sample of the same workload: 4 chunks x 2048 frames,
-    prefill + the workload's full number of greedy steps (or `steps`)."""
+    pinned to the reference's golden tokens) on a bounded sample of the same workload: 4 chunks (2048 frames, or
+    the varlen workload's lengths), prefill + the workload's number of greedy steps (or `steps`).  With per-chunk
+    decode lengths the batch runs until its longest chunk is done, as the reference engine does (finished rows
+    keep computing PAD), and only the bases each chunk emits before its end are counted."""
     import torch
     from oracle import OracleConfig
     from oracle.decoder_torch import TorchCPUModel
@@ -138,16 +159,22 @@ def cpu_baseline(args, cfg, steps=None):
     dc = DecoderConfig(vocab_size=V, rope_theta=1e6)
     tm = TorchCPUModel(OracleConfig(vocab_size=V, rope_theta=1e6), make_weights(dc, seed=0, init="normal"),
                        k=cfg["k"])
-    lens = [PLEN] * B
+    lens = make_lens(cfg, B, seed=7)
+    budgets = make_budgets(dict(cfg, steps=steps), lens)
+    run_steps = steps if budgets is None else max(budgets) + 1
     frames = make_frames(lens, seed=1)
     bias = np.zeros(V, np.float32)
     bias[[0, 1, 2]] = -np.inf
     t0 = time.perf_counter()
-    out = tm.generate(frames, lens, steps, bias, None)
+    out = tm.generate(frames, lens, run_steps, bias, None)
     dt = time.perf_counter() - t0
-    bases = int(tm.tok.n_bases[out].sum())
+    nb = tm.tok.n_bases[out]
+    if budgets is not None:
+        nb = nb * (np.arange(out.shape[1])[None, :] < np.asarray(budgets)[:, None])
+    bases = int(nb.sum())
+    what = f"{PLEN} frames" if cfg["frames"] == "full" else f"frames {lens}, decode lengths {budgets}"
     return {"value": bases / dt, "unit": "bases/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{B} chunks x {PLEN} frames, prefill + {steps} greedy steps, PyTorch CPU fp32 restatement "
+            "sample": f"{B} chunks x {what}, prefill + {run_steps} greedy steps, PyTorch CPU fp32 restatement "
                       f"of the reference path ({dt:.1f} s)", "seconds": dt}
 
 
@@ -169,12 +196,13 @@ def run_reference_arm(args, cfg, rank):
     print(json.dumps(line), flush=True)
 
 
-def attention_roofline(eng, torch, lens, steps):
-    """Average launch time of the decode attention kernel at the mean decode length of the run, timed with
-    CUDA events on the launching stream; algorithmic bytes = K and V rows read + q read + o written."""
+def attention_roofline(eng, torch, mids):
+    """Average launch time of the decode attention kernel with each row at its mean decode length of the run
+    (mids: prefix + 1 + half the row's decode length), timed with CUDA events on the launching stream;
+    algorithmic bytes = K and V rows read + q read + o written."""
     from viktor_b200._lib import call
     B = eng.B
-    mid = torch.tensor([n + 1 + steps // 2 for n in lens], dtype=torch.int32, device=eng.device)
+    mid = torch.tensor(mids, dtype=torch.int32, device=eng.device)
     st = torch.cuda.current_stream(eng.device)
     reps = 5
     kc, vc = eng.cache.k, eng.cache.v
@@ -199,12 +227,12 @@ def attention_roofline(eng, torch, lens, steps):
     return nbytes, t
 
 
-def attention_roofline_i8(eng, torch, lens, steps):
+def attention_roofline_i8(eng, torch, mids):
     """The same measurement for the opt-in int8-prefix kernel (vk_decode_attention_i8): algorithmic bytes =
     int8 prefix (256 B per position) + bf16 tail (512 B per position) + per-channel scales + q read + o written."""
     from viktor_b200._lib import call
     B = eng.B
-    mid = torch.tensor([n + 1 + steps // 2 for n in lens], dtype=torch.int32, device=eng.device)
+    mid = torch.tensor(mids, dtype=torch.int32, device=eng.device)
     st = torch.cuda.current_stream(eng.device)
     reps = 5
     kc, vc = eng.cache.k, eng.cache.v
@@ -244,6 +272,8 @@ def main():
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
     ap.add_argument("--decode-steps", type=int, default=None, help="override the workload's decode steps")
     ap.add_argument("--batch", type=int, default=None, help="override the workload's chunks per GPU (profiling)")
+    ap.add_argument("--engine-batch", type=int, default=None,
+                    help="chunks per DecodeEngine batch (default: the workload's; config 5: 256)")
     ap.add_argument("--decode-groups", type=int, default=2, help="row groups decoded on concurrent streams")
     ap.add_argument("--cpu-steps", type=int, default=None, help="CPU-baseline decode steps (default: workload's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -277,18 +307,34 @@ def main():
     from viktor_b200 import _lib
     from viktor_b200.synthetic import make_weights
 
-    B, steps = cfg["B"], cfg["steps"]
+    B_total, steps = cfg["B"], cfg["steps"]
+    eb = args.engine_batch or cfg.get("engine_batch", B_total)
+    if B_total % eb:
+        raise SystemExit(f"--engine-batch {eb} must divide the {B_total} chunks per GPU")
+    nbat = B_total // eb
     V = 7 if cfg["k"] == 1 else 343
     dcfg = DecoderConfig(vocab_size=V, rope_theta=1e6)
     model = Basecaller.from_weights(make_weights(dcfg, seed=0, init="normal"), k=cfg["k"], cfg=dcfg)
-    lens = make_lens(cfg, B, seed=100 + rank)
-    eng = DecodeEngine(model, B, steps, PLEN, max_homopolymer=None, device=dev, decode_groups=args.decode_groups,
+    lens_all = make_lens(cfg, B_total, seed=100 + rank)
+    budgets_all = make_budgets(cfg, lens_all)
+    eng = DecodeEngine(model, eb, steps, PLEN, max_homopolymer=None, device=dev, decode_groups=args.decode_groups,
                        kv_int8=args.kv_int8)
-    eng.bias[2] = float("-inf")  # EOS masked: fixed-length decode, every step emits a base
+    eng.bias[2] = float("-inf")  # EOS masked: every step emits a base until a chunk's own decode length
+    decode_arg = None if budgets_all is not None else steps  # per-chunk lengths: stop when every chunk ended
     n_bases = torch.as_tensor(model.tokenizer.n_bases, device=dev)
     g = torch.Generator(device=dev)
     g.manual_seed(1 + rank)
-    frames = torch.randn(sum(lens), 512, generator=g, device=dev)
+    frames = torch.randn(sum(lens_all), 512, generator=g, device=dev)
+    offs = np.concatenate([[0], np.cumsum(lens_all)]).astype(np.int64)
+    batches = []  # (frames, lens, decode lengths on the device or None) of each engine batch of this rank
+    for j in range(nbat):
+        lo, hi = j * eb, (j + 1) * eb
+        bud = None if budgets_all is None else torch.tensor(budgets_all[lo:hi], dtype=torch.long, device=dev)
+        batches.append((frames[int(offs[lo]):int(offs[hi])], lens_all[lo:hi], bud))
+
+    def set_budget(bud):
+        if bud is not None:
+            eng.max_tokens.copy_(bud)
 
     def barrier():
         if world > 1:
@@ -297,12 +343,14 @@ def main():
 
     st = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
-        eng.generate(frames, lens, steps)
+        for fr, ln, bud in batches:
+            set_budget(bud)
+            eng.generate(fr, ln, decode_arg)
     eng.check_errors()
 
     # ---- device-resident timed region ----
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps * nbat)]
     bases = torch.zeros((), dtype=torch.long, device=dev)
     launches0 = _lib.launches
     barrier()
@@ -310,13 +358,16 @@ def main():
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_start.record(st)
-        for e0, e1, e2 in ev:
-            e0.record(st)
-            eng.prefill(frames, lens)
-            e1.record(st)
-            out = eng.decode(steps)
-            e2.record(st)
-            bases += n_bases[out].sum()
+        for i in range(args.steps):
+            for j, (fr, ln, bud) in enumerate(batches):
+                e0, e1, e2 = ev[i * nbat + j]
+                set_budget(bud)
+                e0.record(st)
+                eng.prefill(fr, ln)
+                e1.record(st)
+                out = eng.decode(decode_arg)
+                e2.record(st)
+                bases += n_bases[out].sum()
         t_end.record(st)
         barrier()
     launches = _lib.launches - launches0
@@ -332,31 +383,53 @@ def main():
         total_bases = bases_rank
     value = total_bases / elapsed
 
-    # ---- end to end through the public API: pinned host frames in, tokens back to the host ----
+    # ---- end to end through the public API: pinned host frames in, tokens back to one host ----
+    # Every engine batch is generated from pinned host frames (copied per prefill sub-batch inside generate) and
+    # its tokens go into this rank's int16 token array on the device; at the end of the step the arrays of all
+    # ranks are gathered to rank 0 (NCCL) and copied into its pinned host memory, where the bases are counted.
+    # The batches of a shard reuse batch 0's host frames (one pinned engine batch of frames per rank).
     e2e = None
     if not args.no_e2e:
-        host_frames = frames.cpu().pin_memory()
-        host_out = torch.empty(eng.out.shape, dtype=eng.out.dtype).pin_memory()
-        eng.generate(host_frames, lens, steps)
+        from viktor_b200.parallel import gather_tokens, reduce_bench
+        fr0, ln0, _ = batches[0]
+        host_frames = fr0.cpu().pin_memory()
+        tok_dev = torch.empty(B_total, steps, dtype=torch.int16, device=dev)
+        host_tok = torch.empty(world * B_total, steps, dtype=torch.int16).pin_memory() if rank == 0 else None
+        nb_host = np.asarray(model.tokenizer.n_bases)
+
+        def e2e_step():
+            for j, (_, _, bud) in enumerate(batches):
+                set_budget(bud)
+                out = eng.generate(host_frames, ln0, decode_arg)
+                tok_dev[j * eb:(j + 1) * eb].copy_(out)
+            if world > 1:
+                got = gather_tokens(tok_dev, host_out=host_tok)
+            else:
+                host_tok.copy_(tok_dev, non_blocking=True)
+                st.synchronize()
+                got = host_tok
+            return 0 if got is None else int(nb_host[got.numpy()].sum())
+
+        e2e_step()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
         hb = 0
         for _ in range(args.steps):
-            out = eng.generate(host_frames, lens, steps)
-            host_out.copy_(out, non_blocking=True)
-            st.synchronize()
-            hb += int(model.tokenizer.n_bases[host_out.numpy()].sum())
+            hb += e2e_step()
         e1.record(st)
         barrier()
         t_e2e = e0.elapsed_time(e1) / 1e3
         if world > 1:
-            from viktor_b200.parallel import reduce_bench
             t_e2e, _, _, hb = reduce_bench(t_e2e, 0.0, 0.0, hb, dev)
-        e2e = {"value": hb / t_e2e, "unit": "bases/s", "h2d_bytes_per_step": host_frames.numel() * 4,
-               "d2h_bytes_per_step": host_out.numel() * 8}
+        e2e = {"value": hb / t_e2e, "unit": "bases/s", "h2d_bytes_per_step": nbat * host_frames.numel() * 4,
+               "d2h_bytes_per_step": world * B_total * steps * 2,
+               "note": "h2d per rank (fp32 frames, every engine batch); d2h = int16 tokens of all ranks into rank "
+                       "0's pinned memory" + (" after an NCCL gather" if world > 1 else "")}
 
-    nbytes, t_attn = attention_roofline(eng, torch, lens, steps)
+    d0 = budgets_all[:eb] if budgets_all is not None else [steps] * eb
+    mids = [n + 1 + d // 2 for n, d in zip(batches[0][1], d0)]
+    nbytes, t_attn = attention_roofline(eng, torch, mids)
     peak, peak_kind = peaks()
     achieved = nbytes / t_attn / 1e9
     ratio = ncu_traffic_ratio()
@@ -367,7 +440,7 @@ def main():
                 "traffic": None if ratio is None else nbytes * ratio}
     roofline_i8 = None
     if args.kv_int8:
-        nb8, t8 = attention_roofline_i8(eng, torch, lens, steps)
+        nb8, t8 = attention_roofline_i8(eng, torch, mids)
         roofline_i8 = {"bound": "hbm", "kernel": "decode_attn_i8_kernel", "achieved": nb8 / t8 / 1e9, "peak": peak,
                        "unit": "GB/s", "frac": nb8 / t8 / 1e9 / peak, "bytes_per_launch": nb8,
                        "launch_us": t8 * 1e6}
@@ -377,16 +450,21 @@ def main():
         cpu.pop("seconds")
 
     if rank == 0:
+        n_gen = args.steps * nbat
         line = {"metric": "decoded bases/s", "value": value, "unit": "bases/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": cfg["name"], "global_batch": B * world, "seq_len": PLEN + 1 + steps,
-                           "parallelism": f"dp{world} (independent chunk shards)",
-                           "l2": "inputs larger than L2 (KV cache 2 x 8 x B x 3149 x 256 B = 3.3 GB per GPU)"},
-                "decode_us_per_step": decode_s / (args.steps * (steps - 1)) * 1e6,
-                "prefill_ms_per_chunk": prefill_s / (args.steps * B) * 1e3,
+                "config": {"workload": cfg["name"], "global_batch": B_total * world, "engine_batch": eb,
+                           "seq_len": PLEN + 1 + steps, "parallelism": f"dp{world} (independent chunk shards)",
+                           "l2": "inputs larger than L2 (KV cache 2 x 8 x B x 3149 x 256 B = 3.3 GB per 256 chunks)"},
+                "prefill_ms_per_chunk": prefill_s / (n_gen * eb) * 1e3,
                 "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "clocks": clk.summary()}
+        if budgets_all is None:
+            line["decode_us_per_step"] = decode_s / (n_gen * (steps - 1)) * 1e6
+        else:
+            line["decode_ms_per_batch"] = decode_s / n_gen * 1e3
+            line["config"]["decode_lengths"] = "per chunk round(1100 x frames / 2048) tokens, then EOS (max_tokens)"
         if args.kv_int8:
             line["config"]["kv_int8"] = "prefix K/V int8 with per-channel scales, generated tokens bf16"
             line["roofline_int8"] = roofline_i8
