@@ -55,12 +55,12 @@ class TorchCPUModel:
         return x + (F.silu(g) * u) @ self._l(i, "down.weight").T
 
     @torch.no_grad()
-    def generate(self, frames, lens, max_new, bias, max_homopolymer=None):
+    def generate(self, frames, lens, max_new, bias, max_homopolymer=None, return_margin=False):
         """DecodeEngine(backend="torch").generate (viktor/engine.py:168-220) at temperature 0.  Returns out
-        [B, max_new] int64."""
+        [B, max_new] int64 (and with return_margin the fp32 top-2 margin of logits + bias at every selection,
+        [B, max_new], the gap a bf16 path must not cross)."""
         c, tk = self.cfg, self.tok
         B = len(lens)
-        rep = c.n_heads // c.n_kv_heads
         frames = torch.from_numpy(np.ascontiguousarray(frames, dtype=np.float32))
         w = self.w
         prefix = F.gelu(frames @ w["projector.0.weight"].T + w["projector.0.bias"]) @ w["projector.2.weight"].T \
@@ -78,9 +78,8 @@ class TorchCPUModel:
 
             def attend(i, q, k, v, b=b, T=T):
                 Kc[i, b, :T], Vc[i, b, :T] = k[0], v[0]
-                return F.scaled_dot_product_attention(
-                    q.transpose(1, 2), k.transpose(1, 2).repeat_interleave(rep, 1),
-                    v.transpose(1, 2).repeat_interleave(rep, 1), is_causal=True).transpose(1, 2)
+                return F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                                      is_causal=True, enable_gqa=True).transpose(1, 2)
 
             for i in range(c.n_layers):
                 x = self._layer(i, x, cos, sin, attend)
@@ -92,8 +91,13 @@ class TorchCPUModel:
         run = torch.zeros(B, dtype=torch.long)
         head = w["decoder.lm_head.weight"]
 
+        margins = []
+
         def select(logits, prev):
-            nxt = (logits + bias).argmax(-1)
+            z = logits + bias
+            top2 = z.topk(2, -1).values
+            margins.append(top2[:, 0] - top2[:, 1])
+            nxt = z.argmax(-1)
             nxt = torch.where(is_tail[prev], torch.full_like(nxt, EOS), nxt)
             if homo_stop:
                 run.copy_(torch.where((nxt == prev) & is_homo[nxt], run + 1, 0))
@@ -114,9 +118,10 @@ class TorchCPUModel:
             def attend(i, q, k, v):
                 Kc[i, rows, pos], Vc[i, rows, pos] = k[:, 0], v[:, 0]
                 mask = (positions[None, :] <= pos[:, None])[:, None, None, :]
+                n = int(pos.max()) + 1  # positions past every row's current one are masked anyway
                 return F.scaled_dot_product_attention(
-                    q.transpose(1, 2), Kc[i].transpose(1, 2).repeat_interleave(rep, 1),
-                    Vc[i].transpose(1, 2).repeat_interleave(rep, 1), attn_mask=mask).transpose(1, 2)
+                    q.transpose(1, 2), Kc[i, :, :n].transpose(1, 2), Vc[i, :, :n].transpose(1, 2),
+                    attn_mask=mask[..., :n], enable_gqa=True).transpose(1, 2)
 
             for i in range(c.n_layers):
                 x = self._layer(i, x, cos, sin, attend)
@@ -124,4 +129,6 @@ class TorchCPUModel:
             tok = select(h @ head.T, tok)
             out[:, step] = tok
             pos = pos + 1
+        if return_margin:
+            return out.numpy(), torch.stack(margins, 1).numpy()
         return out.numpy()
