@@ -155,3 +155,33 @@ def test_config4_kmer_head_grammar_sampled_rows():
     _report("config 4", ok, identical, stops, steps)
     print(f"config 4: {len(tail_eos)} / {B} rows end with a tail token followed by EOS")
     assert ok.all(), f"rows {np.array(pick)[~ok]} disagree before a low-margin step"
+
+
+def test_config4_long_horizon_sampled_rows():
+    """Config 4 with every row decoding all 280 steps: tails and EOS masked through the bias (the tail rule then
+    never fires), and the head's weights scaled by 16 so that the untrained 343-way logits have fp32 margins
+    above the bf16 floor for most steps (with the plain init they fall below it within a few steps)."""
+    from viktor_b200 import Basecaller, DecodeEngine, DecoderConfig
+    from viktor_b200.config import KmerTokenizer
+    from viktor_b200.synthetic import make_weights
+    B, steps, V = 1024, 280, 343
+    cfg = DecoderConfig(vocab_size=V, rope_theta=1e6)
+    weights = make_weights(cfg, seed=28, init="torch")
+    weights["decoder.lm_head.weight"] = weights["decoder.lm_head.weight"] * 16
+    port = TorchCPUModel(OracleConfig(vocab_size=V, rope_theta=1e6), weights, k=4)
+    model = Basecaller.from_weights(weights, k=4, cfg=cfg)
+    lens = [2048] * B
+    frames = _frames(lens, seed=29)
+    tail = np.asarray(KmerTokenizer(4).tail_mask, dtype=bool)
+    bias = np.zeros(V, np.float32)
+    bias[[0, 1, 2]] = -np.inf
+    bias[tail] = -np.inf
+    eng = DecodeEngine(model, B, steps, 2048, max_homopolymer=None, device="cuda")
+    eng.bias.copy_(torch.from_numpy(bias))
+    got = eng.generate(frames, lens, steps).cpu().numpy()
+    assert (got >= 3).all() and not tail[got].any()
+    pick = [0, 255, 256, 511, 512, 767, 900, B - 1]
+    ref, margin = port.generate(_rows(frames, lens, pick), [2048] * len(pick), steps, bias, None, return_margin=True)
+    ok, identical, stops = _compare(got[pick], ref, margin)
+    _report("config 4 (long horizon)", ok, identical, stops, steps)
+    assert ok.all(), f"rows {np.array(pick)[~ok]} disagree before a low-margin step"
