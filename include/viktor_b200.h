@@ -183,7 +183,8 @@ int vk_linear_rmsnorm(const void* x, const float* ssq, float eps, const void* w_
                       int K, int swiglu, int out_f32, void* stream);
 
 /* q, K/V <- (RMSNorm(x) * w_attn) . W_qkv^T followed by the qkv_rope_cache epilogue (arguments as in
- * vk_qkv_rope_cache; eps is the QK-norm epsilon).  ssq NULL: x is used as given (w_qkv not folded).
+ * vk_qkv_rope_cache; eps is the QK-norm epsilon; q_norm_w and k_norm_w 16-byte aligned).  ssq NULL: x is used
+ * as given (w_qkv not folded).
  * Replaces add_rmsnorm + linear + qkv_rope_cache of viktor/fast_decoder.py:41-47. */
 int vk_linear_qkv_rope_cache(const void* x, const float* ssq, float norm_eps, const void* w_qkv,
                              const void* q_norm_w, const void* k_norm_w, const float* cos, const float* sin,

@@ -284,10 +284,14 @@ VK_DEV float group8_sum(float v) {
 }
 
 // Epilogue inputs of one thread's reduced row (split-K), loaded before the accumulator is ready.
+// Everything the epilogue reads from global memory is loaded here, before the accumulator wait, for every pass
+// a thread makes (up to two): under a saturated memory system each such load is a long round trip, so none may
+// sit between the split-K exchange and the stores.
 struct RowInputs {
   float r;                       // folded-norm row scale
   int pos, rpos, seq;            // QKV_ROPE
   float c[8], s[8];              // QKV_ROPE: cos / sin of the eight rotation angles this thread applies
+  float wn[8];                   // QKV_ROPE: the QK-norm weights of this thread's eight columns of its head
   float xres[8];                 // ADD_RESID: this thread's eight residual columns
 };
 
@@ -311,6 +315,13 @@ VK_DEV RowInputs load_row_inputs(const EpiArgs& ep, int row, int n_tile, int g8,
     in.c[4] = c1.x; in.c[5] = c1.y; in.c[6] = c1.z; in.c[7] = c1.w;
     in.s[0] = s0.x; in.s[1] = s0.y; in.s[2] = s0.z; in.s[3] = s0.w;
     in.s[4] = s1.x; in.s[5] = s1.y; in.s[6] = s1.z; in.s[7] = s1.w;
+    const int gh = n_tile * (BN / 64) + g8 / 8;  // head of this thread's columns
+    if (gh < ep.n_heads + ep.n_kv_heads) {
+      load_bf16x8((gh < ep.n_heads ? ep.q_norm_w : ep.k_norm_w) + (g8 & 7) * 8, in.wn);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) in.wn[i] = 0.f;
+    }
   }
   if (EPI == ADD_RESID) {
     if (valid) {
@@ -390,10 +401,9 @@ VK_DEV void epi_group8(const EpiArgs& ep, int row, int n_tile, int g8, float* v,
       for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
       ss = group8_sum(ss);
       const float rr = rsqrtf(ss * (1.0f / 64.0f) + ep.qk_eps);
-      const __nv_bfloat16* wn = gh < H ? ep.q_norm_w : ep.k_norm_w;
       float y[8], other[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = bf16_round(v[i] * rr * __bfloat162float(wn[j * 8 + i]));
+      for (int i = 0; i < 8; ++i) y[i] = bf16_round(v[i] * rr * in.wn[i]);
 #pragma unroll
       for (int i = 0; i < 8; ++i) other[i] = __shfl_xor_sync(0xffffffffu, y[i], 4);
 #pragma unroll
@@ -615,10 +625,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     static_assert(SLICE % 16 == 0, "bulk copies move multiples of 16 bytes");
     const int t = epi_warp ? static_cast<int>(threadIdx.x) - 64 : 0;
     const int g8 = t & (TPR - 1);
-    RowInputs in;
+    RowInputs in0, in1;  // the inputs of passes 0 and 1
     if (epi_warp) {
-      const int rl = t / TPR, row = m0 + ks * R + rl;
-      in = load_row_inputs<BN, EPI>(ep, row, n_tile, g8, N, rl < R && row < M);
+      const int rl0 = t / TPR, row0 = m0 + ks * R + rl0;
+      in0 = load_row_inputs<BN, EPI>(ep, row0, n_tile, g8, N, rl0 < R && row0 < M);
+      if (PASSES > 1) {
+        const int rl1 = RPP + t / TPR, row1 = m0 + ks * R + rl1;
+        in1 = load_row_inputs<BN, EPI>(ep, row1, n_tile, g8, N, rl1 < R && row1 < M);
+      }
     }
     wait_accum();
     if (epi_warp) {
@@ -651,12 +665,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!got && t == 0) raise_error(ERR_WAIT_FULL);
       __syncwarp();
       cluster_arrive();                             // (phase B) this CTA's slices have all arrived
-#pragma unroll 1
-      for (int pass = 0; pass < PASSES; ++pass) {
+      auto do_pass = [&](int pass, const RowInputs& in) {
         const int rl = pass * RPP + t / TPR;
         const int row = m0 + ks * R + rl;
         const bool active = have_acc && got && rl < R && row < M;
-        if (pass > 0) in = load_row_inputs<BN, EPI>(ep, row, n_tile, g8, N, rl < R && row < M);
         const int rs = rl < R ? rl : 0;
         float v[NV];
 #pragma unroll
@@ -675,6 +687,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         epi_group8<BN, EPI>(ep, row, n_tile, g8, v, in, N, active);
+      };
+      do_pass(0, in0);
+      if (PASSES > 1) do_pass(1, in1);
+#pragma unroll 1
+      for (int pass = 2; pass < PASSES; ++pass) {  // (more than two passes: wide tiles with few splits)
+        const int rl = pass * RPP + t / TPR, row = m0 + ks * R + rl;
+        do_pass(pass, load_row_inputs<BN, EPI>(ep, row, n_tile, g8, N, rl < R && row < M));
       }
     } else {
       __syncwarp();

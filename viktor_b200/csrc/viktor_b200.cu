@@ -731,7 +731,7 @@ int vk_linear_qkv_rope_cache(const void* x, const float* ssq, float norm_eps, co
     return VK_ERR_ARG;
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || stride_cs % 8 || stride_cb % 8 ||
       !aligned16(cos) || !aligned16(sin) || (k_out && !aligned16(k_out)) || (v_out && !aligned16(v_out)) ||
-      (ssq && !aligned16(ssq)))
+      (ssq && !aligned16(ssq)) || !aligned16(q_norm_w) || !aligned16(k_norm_w))
     return VK_ERR_ARG;
   gemm::EpiArgs ep = epi_zero();
   ep.ssq_in = ssq;
