@@ -664,7 +664,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool got = mbar_wait(recv_bar, 0);
       if (!got && t == 0) raise_error(ERR_WAIT_FULL);
       __syncwarp();
-      cluster_arrive();                             // (phase B) this CTA's slices have all arrived
+      cluster_arrive_relaxed();                     // (phase B) this CTA's slices have all arrived
       auto do_pass = [&](int pass, const RowInputs& in) {
         const int rl = pass * RPP + t / TPR;
         const int row = m0 + ks * R + rl;
@@ -697,8 +697,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else {
       __syncwarp();
-      cluster_wait();    // (phase A)
-      cluster_arrive();  // (phase B)
+      cluster_wait();            // (phase A)
+      cluster_arrive_relaxed();  // (phase B)
     }
     __syncwarp();
     cluster_wait();  // (phase B) every slice of the cluster has landed: no copy still reads this CTA's staging

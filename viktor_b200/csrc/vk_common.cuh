@@ -190,6 +190,9 @@ VK_DEV void cluster_sync() {
 // The two halves of cluster_sync, for work that can sit between arriving and waiting.
 VK_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 VK_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// An arrive that publishes no memory of this thread (no release fence): for barriers that only order the lifetime
+// of shared memory read by copies whose completion the arriving thread has already observed on an mbarrier.
+VK_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 VK_DEV uint32_t dsmem_addr(const void* local_smem_ptr, uint32_t rank) {
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local_smem_ptr)), "r"(rank));
