@@ -15,6 +15,10 @@ namespace vk {
 
 static int g_pdl = 1;
 
+#ifndef VK_ATTN_MAX_CHUNK
+#define VK_ATTN_MAX_CHUNK 1024
+#endif
+
 // Per-device record of kernels whose dynamic shared-memory limit has been raised.  The first launch of each
 // kernel on a device must happen outside stream capture (engines warm up eagerly before capturing).
 template <typename K>
@@ -496,8 +500,9 @@ int vk_decode_attention(const void* q, const void* k_cache, const void* v_cache,
   const int splits = (S + attn::kMinChunk - 1) / attn::kMinChunk;  // workspace slots per query
   const int sms = device_sm_count();
   if (sms <= 0) return VK_ERR_CUDA;
-  // longest split that still fills every SM with its two resident CTAs (judged on the cache length)
-  int chunk = 1024;
+  // longest split that still fills every SM with its two resident CTAs (judged on the cache length); at most
+  // VK_ATTN_MAX_CHUNK positions (a build-time tuning constant)
+  int chunk = VK_ATTN_MAX_CHUNK;
   while (chunk > attn::kMinChunk && static_cast<int64_t>(nq) * ((S + chunk - 1) / chunk) < 2 * sms) chunk /= 2;
   attn::DecodeArgs a;
   memset(&a, 0, sizeof(a));
