@@ -228,21 +228,25 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         tc_fence_after();
       }
-      // P_j = exp2(s * scale - mu) (bf16) into TMEM, 32 keys per store; partial row sums for ILP
-      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // P_j = exp2(s * scale - mu) (bf16) into TMEM, 32 keys per store; partial row sums for ILP.  Scores are
+      // taken in pairs with packed fp32x2 arithmetic (the softmax warps are bound by their instruction issue: an
+      // FMA-pipe polynomial for part of the exponentials, to unload MUFU, measured slower).
+      const float2 sc2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-mu, -mu);
+      float2 rs4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int c0 = 0; c0 < kBK; c0 += 32) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float p0 = fast_exp2(fmaf(v[c0 + i], a.scale_log2, -mu));
-          const float p1 = fast_exp2(fmaf(v[c0 + i + 1], a.scale_log2, -mu));
-          rs8[(i >> 1) & 7] += p0 + p1;
-          pk[i / 2] = pack_bf16x2(p0, p1);
+          const float2 t = __ffma2_rn(make_float2(v[c0 + i], v[c0 + i + 1]), sc2, nm2);
+          const float2 p = make_float2(fast_exp2(t.x), fast_exp2(t.y));
+          rs4[(i >> 1) & 3] = __fadd2_rn(rs4[(i >> 1) & 3], p);
+          pk[i / 2] = pack_bf16x2(p.x, p.y);
         }
         tmem_st16(trow + kColP + c0 / 2, pk);
       }
-      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+      const float2 rs2 = __fadd2_rn(__fadd2_rn(rs4[0], rs4[1]), __fadd2_rn(rs4[2], rs4[3]));
+      const float rs = rs2.x + rs2.y;
       // rescale the accumulator when this warp's row maxima moved (alpha = 1 otherwise)
       if (j >= 1 && !__all_sync(0xffffffffu, alpha == 1.f)) {
         float o[64];
