@@ -9,8 +9,8 @@ N(0, 0.02) random weights, bf16.  Other BASELINE configs:
     --config 3   512 chunks of U{128..2048 step 128} frames; chunk b decodes round(1100 x frames_b / 2048)
                  tokens, then EOS and PAD (engine.max_tokens); decode(steps=None) stops when every chunk ended
     --config 4   1024 chunks x 2048 frames, 4-mer vocabulary (343), 280 steps
-    --config 5   2048 chunks per GPU (config-2 lengths) in engine batches of 256 (--engine-batch), all ranks'
-                 tokens gathered to rank 0's host
+    --config 5   2048 chunks per GPU (config-2 lengths) in one engine batch of 2048 (--engine-batch 256: eight
+                 batches of config 2's size), all ranks' tokens gathered to rank 0's host
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
 
@@ -49,7 +49,7 @@ CONFIGS = {
     4: dict(name="config4: 1024 chunks x 2048 frames, 280 greedy steps, 4-mer vocab 343", B=1024, frames="full",
             steps=280, k=4),
     5: dict(name="config5: 2048 chunks per GPU x 2048 frames (config-2 lengths), 1100 greedy steps, vocab 7, "
-                 "tokens of every rank gathered to rank 0's host", B=2048, engine_batch=256, frames="full",
+                 "tokens of every rank gathered to rank 0's host", B=2048, engine_batch=2048, frames="full",
             steps=1100, k=1),
 }
 PLEN = 2048
@@ -273,7 +273,7 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=None, help="override the workload's decode steps")
     ap.add_argument("--batch", type=int, default=None, help="override the workload's chunks per GPU (profiling)")
     ap.add_argument("--engine-batch", type=int, default=None,
-                    help="chunks per DecodeEngine batch (default: the workload's; config 5: 256)")
+                    help="chunks per DecodeEngine batch (default: the workload's; config 5: 2048)")
     ap.add_argument("--decode-groups", type=int, default=2, help="row groups decoded on concurrent streams")
     ap.add_argument("--cpu-steps", type=int, default=None, help="CPU-baseline decode steps (default: workload's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
