@@ -159,8 +159,10 @@ def test_config4_kmer_head_grammar_sampled_rows():
 
 def test_config4_long_horizon_sampled_rows():
     """Config 4 with every row decoding all 280 steps: tails and EOS masked through the bias (the tail rule then
-    never fires), and the head's weights scaled by 16 so that the untrained 343-way logits have fp32 margins
-    above the bf16 floor for most steps (with the plain init they fall below it within a few steps)."""
+    never fires), and the head's weights scaled by 16.  Scaling the head scales the logits' bf16 errors as much as
+    their margins, so the margin floor is scaled with it (16 x 0.05): the comparison is as strict as the plain
+    one, over rows that keep decoding to the end (with the untrained 343-way head, near-ties limit how far a row
+    can be compared, whatever the scale)."""
     from viktor_b200 import Basecaller, DecodeEngine, DecoderConfig
     from viktor_b200.config import KmerTokenizer
     from viktor_b200.synthetic import make_weights
@@ -182,6 +184,6 @@ def test_config4_long_horizon_sampled_rows():
     assert (got >= 3).all() and not tail[got].any()
     pick = [0, 255, 256, 511, 512, 767, 900, B - 1]
     ref, margin = port.generate(_rows(frames, lens, pick), [2048] * len(pick), steps, bias, None, return_margin=True)
-    ok, identical, stops = _compare(got[pick], ref, margin)
+    ok, identical, stops = _compare(got[pick], ref, margin / 16.0)
     _report("config 4 (long horizon)", ok, identical, stops, steps)
     assert ok.all(), f"rows {np.array(pick)[~ok]} disagree before a low-margin step"

@@ -71,7 +71,7 @@ class DecodeEngine:
     def __init__(self, model, batch_size: int, max_new_tokens: int, max_frames: int, backend: str = "auto",
                  cuda_graph: bool = True, prefill_batch: int = 128, check_every: int = 32,
                  attention_backend: str = "auto", temperature: float = 0.0, max_homopolymer: int | None = 64,
-                 device=None, decode_groups: int = 2, kv_int8: bool = False):
+                 device=None, decode_groups: int = 2, kv_int8: bool = False, steps_per_graph: int = 16):
         if backend not in ("auto", "cuda", "triton"):
             raise ValueError(f"backend {backend!r}: this engine runs the B200 CUDA kernels only")
         if attention_backend not in ("auto", "cuda", "triton", "flash"):
@@ -168,7 +168,9 @@ class DecodeEngine:
             self._ws8 = [torch.zeros(load().vk_decode_attention_i8_workspace_bytes(hi - lo, S8, self.max_tail),
                                      dtype=torch.uint8, device=dev) for lo, hi, _ in self._groups]
         self.graph = None
+        self.graph_multi = None
         self.kernels_per_step = 0
+        self.steps_per_graph = max(1, int(steps_per_graph))
         if cuda_graph:
             self._capture()
 
@@ -193,6 +195,24 @@ class DecodeEngine:
             side.wait_stream(main)
             with torch.cuda.stream(side):
                 self._step_rows(gi, side.cuda_stream)
+        for side in self._side_streams:
+            main.wait_stream(side)
+
+    def _steps(self, n):
+        """n decode steps.  Greedy steps of several groups run each group's n steps back to back on its own stream
+        (the groups' rows are independent); sampled steps draw their noise for all rows per step, so they go through
+        _step one at a time."""
+        if self.noise is not None or not self._side_streams:
+            for _ in range(n):
+                self._step()
+            return
+        main = torch.cuda.current_stream(self.device)
+        for side in self._side_streams:
+            side.wait_stream(main)
+        for _ in range(n):
+            for gi, side in enumerate(self._side_streams):
+                with torch.cuda.stream(side):
+                    self._step_rows(gi, side.cuda_stream)
         for side in self._side_streams:
             main.wait_stream(side)
 
@@ -247,6 +267,14 @@ class DecodeEngine:
         with torch.cuda.graph(self.graph):
             self._step()
         self.kernels_per_step = _lib.launches - before
+        # Several steps in one graph: between two graph launches the GPU idles (~13 us measured at config 2), while
+        # inside a graph each decode group's next step follows its previous one on the same stream, its kernels
+        # launched early (programmatic dependent launch) as within a step.
+        self.graph_multi = None
+        if self.steps_per_graph > 1:
+            self.graph_multi = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph_multi):
+                self._steps(self.steps_per_graph)
         for t, v in zip((self.pos, self.pos32, self.seqlens, self.rpos32, self.tok, self.run), saved):
             t.copy_(v)
         self.out.fill_(PAD)
@@ -395,14 +423,23 @@ class DecodeEngine:
         """Run decode steps after prefill.  steps=None: stop when all sequences ended (checked every check_every
         steps) or at max_new_tokens.  steps=n: run exactly n-1 steps (n output tokens)."""
         n = self.max_new - 1 if steps is None else steps - 1
-        for i in range(n):
-            if self.graph is not None:
+        k = self.steps_per_graph if self.graph_multi is not None else 1
+        if steps is None and self.check_every % k:
+            k = 1  # the multi-step graph must not step past a check_every poll
+        i = 0
+        while i < n:
+            if self.graph is None:
+                self._step()
+                i += 1
+            elif k > 1 and n - i >= k:
+                self.graph_multi.replay()
+                _lib.launches += k * self.kernels_per_step
+                i += k
+            else:
                 self.graph.replay()
                 _lib.launches += self.kernels_per_step
-            else:
-                self._step()
-            if steps is None and (i + 1) % self.check_every == 0 and bool(
-                    ((self.tok == EOS) | (self.tok == PAD)).all()):
+                i += 1
+            if steps is None and i % self.check_every == 0 and bool(((self.tok == EOS) | (self.tok == PAD)).all()):
                 break
         return self.out
 
