@@ -162,6 +162,11 @@ int vk_decode_attention_noalloc(const void* q, const void* k_cache, const void* 
                                 void* out, int nq, int row0, int cache_rows, int S, int64_t stride_kb,
                                 int64_t stride_ks, void* stream);
 
+/* Test hook: fills the current device's noalloc tickets with a nonzero byte pattern on `stream`, the state an
+ * aborted call could leave behind, so that a test can check that the next vk_decode_attention_noalloc clears
+ * them (stale tickets would keep every split from merging and leave the output unwritten). */
+int vk_test_noalloc_poison(void* stream);
+
 /* flash_attn_varlen_func(q, k, v, cu, cu, max_len, max_len, causal=True) of viktor/fast_decoder.py:73, with K
  * and V read from the cache rows the prefill just wrote.  q, out [n_tok, 8, 64] bf16 packed by cu_seqlens
  * [nseq + 1] (i32, device); sequence b attends cache row row0 + b, positions [0, T_b).  max_seqlen = max T_b. */

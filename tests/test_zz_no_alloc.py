@@ -68,6 +68,24 @@ def test_noalloc_matches_workspace_entry_point_twice():
         assert (ref.float() - exact).abs().max().item() < 0.01
 
 
+def test_noalloc_clears_stale_tickets():
+    """An earlier call that stopped before its merge leaves tickets set; the next call must clear them itself."""
+    from viktor_b200._lib import call, check_device_errors, load
+    lib = load()
+    q, k, v, lens = _inputs(2, 128, 2600)
+    ws = torch.zeros(lib.vk_decode_attention_workspace_bytes(128, 2600), dtype=torch.uint8, device="cuda")
+    ref = _run("vk_decode_attention", q, k, v, lens, ws)
+    stream = torch.cuda.current_stream().cuda_stream
+    call("vk_test_noalloc_poison", stream)
+    got = torch.full_like(q, float("nan"))  # rows that never merged would keep the NaN
+    call("vk_decode_attention_noalloc", q.data_ptr(), k.data_ptr(), v.data_ptr(), lens.data_ptr(), got.data_ptr(),
+         128, 0, 128, 2600, k.stride(0), k.stride(1), stream)
+    torch.cuda.synchronize()
+    check_device_errors()
+    assert not got.isnan().any()
+    assert (got.float() - ref.float()).abs().max().item() < 0.01
+
+
 def test_noalloc_rejects_sizes_beyond_its_array():
     from viktor_b200._lib import VK_ERR_ARG, load
     lib = load()

@@ -22,6 +22,7 @@ _SIGS = {
     "vk_read_device_errors": (i32, [C.POINTER(C.c_uint32), i32]),
     "vk_set_pdl": (i32, [i32]),
     "vk_test_bounded_wait": (i32, [C.c_uint64, p, p]),
+    "vk_test_noalloc_poison": (i32, [p]),
     "vk_add_rmsnorm": (i32, [p, p, p, p, i64, i32, f32, p]),
     "vk_embed_rmsnorm": (i32, [p, p, i64, p, p, p, i64, i32, f32, p]),
     "vk_qkv_rope_cache": (i32, [p, p, p, p, p, i32, p, p, p, p, p, p, p, p, i64, i64, i64, i32, i32, f32, i32, i32,

@@ -693,6 +693,14 @@ int vk_decode_attention_noalloc(const void* q, const void* k_cache, const void* 
                              scratch[dev], vk::kNoAllocBytes, stream);
 }
 
+int vk_test_noalloc_poison(void* stream) {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, vk::g_noalloc_attn_scratch) != cudaSuccess || !p) return VK_ERR_CUDA;
+  const size_t tickets = static_cast<size_t>(vk::kNoAllocMaxQ) * 4;
+  if (cudaMemsetAsync(p, 0x5A, tickets, static_cast<cudaStream_t>(stream)) != cudaSuccess) return VK_ERR_CUDA;
+  return VK_OK;
+}
+
 int vk_prefill_attention(const void* q, const void* k_cache, const void* v_cache, const int32_t* cu_seqlens,
                          int nseq, int max_seqlen, int64_t n_tok, int row0, int cache_rows, int S,
                          int64_t stride_kb, int64_t stride_ks, void* out, void* stream) {
