@@ -56,6 +56,40 @@ def test_align_matches_oracle():
         assert got == exp, (q, t, mode, k, got, exp)
 
 
+def test_align_distances_match_an_independent_matcher():
+    """Edit distances of all three modes against the `regex` package's fuzzy matching (its own implementation,
+    not derived from this code base or the oracle): the least k for which the query matches with at most k
+    errors, anchored at both ends (NW), at the start (SHW) or anywhere (HW).  Distances up to 6 only: the fuzzy
+    search grows exponentially in k."""
+    regex = pytest.importorskip("regex")
+    from viktor_b200.stitch import HW, NW, SHW, align
+
+    def least_k(q, t, mode, kmax=6):
+        find = {NW: regex.fullmatch, SHW: regex.match, HW: regex.search}[mode]
+        for k in range(kmax + 1):
+            if find("(?:%s){e<=%d}" % (q, k), t, timeout=5.0) is not None:
+                return k
+        return None
+
+    rng = np.random.default_rng(1)
+    checked = 0
+    for _ in range(300):
+        q = _rand_seq(rng, int(rng.integers(4, 24)))
+        core = _mutate(rng, q, 0.15)
+        for mode in (NW, SHW, HW):
+            t = core
+            if mode == SHW:
+                t = core + _rand_seq(rng, int(rng.integers(0, 8)))
+            elif mode == HW:
+                t = _rand_seq(rng, int(rng.integers(0, 8))) + core + _rand_seq(rng, int(rng.integers(0, 8)))
+            exp = least_k(q, t, mode)
+            if exp is None:
+                continue
+            assert align(q, t, mode)["editDistance"] == exp, (q, t, mode)
+            checked += 1
+    assert checked > 800
+
+
 def test_overlap_cut_matches_oracle():
     from viktor_b200.stitch import overlap_cut
     rng = np.random.default_rng(1)
