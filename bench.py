@@ -51,8 +51,7 @@ CONFIGS = {
     5: dict(name="config5: 2048 chunks per GPU x 2048 frames (config-2 lengths), 1100 greedy steps, vocab 7, "
                  "tokens of every rank gathered to rank 0's host", B=2048, engine_batch=2048, frames="full",
             steps=1100, k=1),
-    # the survey's reading of config 5: the config-3 workload (varlen prefixes, per-chunk decode lengths) at
-    # 2048 chunks per GPU
+    # config 5 with the config-3 workload (varlen prefixes, per-chunk decode lengths) at 2048 chunks per GPU
     6: dict(name="config5 with config-3 lengths: 2048 chunks per GPU x U{128..2048 step 128} frames, decode "
                  "length 1100 x frames / 2048 (then EOS, PAD), vocab 7, tokens of every rank gathered to rank 0's "
                  "host", B=2048, engine_batch=2048, frames="varlen", steps=1100, k=1, budget=True),

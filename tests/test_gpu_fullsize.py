@@ -1,9 +1,9 @@
-"""Parity at the benchmark sizes (3 and 4), on sampled rows.
+"""Parity at the benchmark sizes (configs 2, 3 and 4 of the benchmark), on sampled rows.
 
 The engine decodes the whole batch at the benchmark shape on the GPU; a sample of its rows is decoded again by
 the pinned PyTorch CPU port of the reference (oracle/decoder_torch.py, fp32, tokens equal to the reference's on
-every golden case).  Weights follow SURVEY D3 (PyTorch-default init: the benchmark's N(0, 0.02) init is
-degenerate for token parity).  Rule, as in the golden-case tests: every sampled row agrees with the fp32 tokens
+every golden case).  Weights use the PyTorch-default init (the benchmark's N(0, 0.02) init is degenerate
+for token parity).  Rule, as in the golden-case tests: every sampled row agrees with the fp32 tokens
 up to its first step whose fp32 top-2 margin is below the bf16 noise floor (0.05); the share of rows identical
 over all steps is printed (with this untrained init some rows meet an fp32 near-tie, where any bf16 path may
 take the other token).
