@@ -11,8 +11,9 @@ N(0, 0.02) random weights, bf16.  Other BASELINE configs:
     --config 4   1024 chunks x 2048 frames, 4-mer vocabulary (343), 280 steps
     --config 5   2048 chunks per GPU (config-2 lengths) in one engine batch of 2048 (--engine-batch 256: eight
                  batches of config 2's size), all ranks' tokens gathered to rank 0's host
+    --config 6   config 5 with the config-3 workload (varlen prefixes, per-chunk decode lengths)
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5|6]
 
 Multi-GPU: one process per GPU under torch.distributed.run; every rank runs its own engine on its own chunks
 (weak scaling, no collective on the data path); the barrier / max-over-ranks timing uses NCCL, and in the e2e
