@@ -143,12 +143,95 @@ VK_DEV void norm_rope_head(float* v, const __nv_bfloat16* w, const float* c, con
   const float ss = ((ss8[0] + ss8[1]) + (ss8[2] + ss8[3])) + ((ss8[4] + ss8[5]) + (ss8[6] + ss8[7]));
   const float r = rsqrtf(ss * (1.0f / 64.0f) + eps);
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float y1 = bf16_round(v[i] * r * __bfloat162float(w[i]));
-    const float y2 = bf16_round(v[i + 32] * r * __bfloat162float(w[i + 32]));
-    v[i] = y1 * c[i] - y2 * s[i];
-    v[i + 32] = y1 * s[i] + y2 * c[i];
+  for (int i = 0; i < 32; i += 8) {
+    float wa[8], wb[8];  // 16-byte loads of the norm weights (the pointer is 16-byte aligned)
+    load_bf16x8(w + i, wa);
+    load_bf16x8(w + i + 32, wb);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float y1 = bf16_round(v[i + e] * r * wa[e]);
+      const float y2 = bf16_round(v[i + e + 32] * r * wb[e]);
+      v[i + e] = y1 * c[i + e] - y2 * s[i + e];
+      v[i + e + 32] = y1 * s[i + e] + y2 * c[i + e];
+    }
   }
+}
+
+// Per-row inputs of the QKV_ROPE epilogue (cache position, RoPE position, cache row, the cos / sin row), loaded
+// once per row so that a caller can fetch them before its accumulator is ready.
+struct QkvRow {
+  int p, rp, sq;
+  bool ok;  // every index in range
+  float c[32], s[32];
+};
+
+VK_DEV void load_qkv_row(const EpiArgs& ep, int row, QkvRow& q) {
+  q.p = ep.pos[row];
+  q.rp = ep.rope_pos ? ep.rope_pos[row] : q.p;
+  q.sq = ep.seq[row];
+  q.ok = q.p >= 0 && q.p < ep.cache_len && q.sq >= 0 && q.sq < ep.cache_rows && q.rp >= 0 && q.rp < ep.rope_len;
+  const int64_t rp = q.ok ? q.rp : 0;
+  const float4* cp = reinterpret_cast<const float4*>(ep.cos + rp * 32);
+  const float4* sp = reinterpret_cast<const float4*>(ep.sin + rp * 32);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 a = cp[i], b = sp[i];
+    q.c[4 * i] = a.x; q.c[4 * i + 1] = a.y; q.c[4 * i + 2] = a.z; q.c[4 * i + 3] = a.w;
+    q.s[4 * i] = b.x; q.s[4 * i + 1] = b.y; q.s[4 * i + 2] = b.z; q.s[4 * i + 3] = b.w;
+  }
+}
+
+// QKV_ROPE epilogue of global head gh (64 values in v, row scale r): round to bf16, QK-norm + RoPE for q and k
+// heads, then q to q_out and k / v into the cache (and the packed copies when asked).
+VK_DEV void qkv_head(const EpiArgs& ep, int row, int gh, float* v, float r, const QkvRow& q) {
+  const int H = ep.n_heads, HKV = ep.n_kv_heads;
+  if (!q.ok) {
+    raise_error(ERR_BOUNDS);
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = bf16_round(v[i] * r);  // the qkv linear output is stored in bf16
+  if (gh < H + HKV) norm_rope_head(v, gh < H ? ep.q_norm_w : ep.k_norm_w, q.c, q.s, ep.qk_eps);
+  if (gh < H) {
+    __nv_bfloat16* qp = ep.q_out + (static_cast<int64_t>(row) * H + gh) * 64;
+#pragma unroll
+    for (int i = 0; i < 64; i += 8) store_bf16x8(qp + i, v + i);
+  } else if (gh < H + 2 * HKV) {
+    const bool is_k = gh < H + HKV;
+    const int kvh = is_k ? gh - H : gh - H - HKV;
+    __nv_bfloat16* cache = is_k ? ep.k_cache : ep.v_cache;
+    __nv_bfloat16* dst =
+        cache + static_cast<int64_t>(q.sq) * ep.stride_cb + static_cast<int64_t>(q.p) * ep.stride_cs + kvh * 64;
+#pragma unroll
+    for (int i = 0; i < 64; i += 8) store_bf16x8(dst + i, v + i);
+    __nv_bfloat16* packed = is_k ? ep.k_out : ep.v_out;
+    if (packed) {
+      __nv_bfloat16* pd = packed + (static_cast<int64_t>(row) * HKV + kvh) * 64;
+#pragma unroll
+      for (int i = 0; i < 64; i += 8) store_bf16x8(pd + i, v + i);
+    }
+  }
+}
+
+// ADD_RESID epilogue of the 64 columns c0.. of one row: x += bf16(v) (bf16 rounding), with the residual's 64
+// bf16 values given in xr (loaded by the caller), and the block's sum of squares to ssq_out.
+VK_DEV void add_resid_block(const EpiArgs& ep, int row, int c0, const float* v, const uint4* xr, int N) {
+  __nv_bfloat16* xp = ep.x + static_cast<int64_t>(row) * N + c0;
+  float ss8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent chains (see norm_rope_head)
+#pragma unroll
+  for (int i = 0; i < 64; i += 8) {
+    const uint4 u = xr[i / 8];
+    float xo[8] = {bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y),
+                   bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w)};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      xo[e] = bf16_round(xo[e] + bf16_round(v[i + e]));
+      ss8[e] = fmaf(xo[e], xo[e], ss8[e]);
+    }
+    store_bf16x8(xp + i, xo);
+  }
+  ep.ssq_out[static_cast<int64_t>(row) * kSsqSlots + c0 / 64] =
+      ((ss8[0] + ss8[1]) + (ss8[2] + ss8[3])) + ((ss8[4] + ss8[5]) + (ss8[6] + ss8[7]));
 }
 
 // Number of epilogue chunks of a BN tile and their width.  A chunk is 64 consecutive columns (BN < 64: BN
@@ -211,64 +294,15 @@ VK_DEV void epi_chunk(const EpiArgs& ep, int row, int n_tile, int ch, float* v, 
     }
   } else if (EPI == ADD_RESID) {
     const int c0 = n_tile * BN + ch * 64;
-    __nv_bfloat16* xp = ep.x + static_cast<int64_t>(row) * N + c0;
-    float ss8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent chains (see norm_rope_head)
+    const uint4* xp = reinterpret_cast<const uint4*>(ep.x + static_cast<int64_t>(row) * N + c0);
+    uint4 xr[8];
 #pragma unroll
-    for (int i = 0; i < 64; i += 8) {
-      float xo[8];
-      load_bf16x8(xp + i, xo);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        xo[e] = bf16_round(xo[e] + bf16_round(v[i + e]));
-        ss8[e] = fmaf(xo[e], xo[e], ss8[e]);
-      }
-      store_bf16x8(xp + i, xo);
-    }
-    ep.ssq_out[static_cast<int64_t>(row) * kSsqSlots + c0 / 64] =
-        ((ss8[0] + ss8[1]) + (ss8[2] + ss8[3])) + ((ss8[4] + ss8[5]) + (ss8[6] + ss8[7]));
+    for (int i = 0; i < 8; ++i) xr[i] = xp[i];
+    add_resid_block(ep, row, c0, v, xr, N);
   } else if (EPI == QKV_ROPE) {
-    const int H = ep.n_heads, HKV = ep.n_kv_heads;
-    const int gh = n_tile * (BN / 64) + ch;
-    const int p = ep.pos[row];
-    const int rp = ep.rope_pos ? ep.rope_pos[row] : p;
-    const int sq = ep.seq[row];
-    if (p < 0 || p >= ep.cache_len || sq < 0 || sq >= ep.cache_rows || rp < 0 || rp >= ep.rope_len) {
-      raise_error(ERR_BOUNDS);
-      return;
-    }
-#pragma unroll
-    for (int i = 0; i < 64; ++i) v[i] = bf16_round(v[i] * r);  // the qkv linear output is stored in bf16
-    if (gh < H + HKV) {
-      float c[32], s[32];
-      const float4* cp = reinterpret_cast<const float4*>(ep.cos + static_cast<int64_t>(rp) * 32);
-      const float4* sp = reinterpret_cast<const float4*>(ep.sin + static_cast<int64_t>(rp) * 32);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 a = cp[i], b = sp[i];
-        c[4 * i] = a.x; c[4 * i + 1] = a.y; c[4 * i + 2] = a.z; c[4 * i + 3] = a.w;
-        s[4 * i] = b.x; s[4 * i + 1] = b.y; s[4 * i + 2] = b.z; s[4 * i + 3] = b.w;
-      }
-      norm_rope_head(v, gh < H ? ep.q_norm_w : ep.k_norm_w, c, s, ep.qk_eps);
-    }
-    if (gh < H) {
-      __nv_bfloat16* qp = ep.q_out + (static_cast<int64_t>(row) * H + gh) * 64;
-#pragma unroll
-      for (int i = 0; i < 64; i += 8) store_bf16x8(qp + i, v + i);
-    } else if (gh < H + 2 * HKV) {
-      const bool is_k = gh < H + HKV;
-      const int kvh = is_k ? gh - H : gh - H - HKV;
-      __nv_bfloat16* cache = is_k ? ep.k_cache : ep.v_cache;
-      __nv_bfloat16* dst =
-          cache + static_cast<int64_t>(sq) * ep.stride_cb + static_cast<int64_t>(p) * ep.stride_cs + kvh * 64;
-#pragma unroll
-      for (int i = 0; i < 64; i += 8) store_bf16x8(dst + i, v + i);
-      __nv_bfloat16* packed = is_k ? ep.k_out : ep.v_out;
-      if (packed) {
-        __nv_bfloat16* pd = packed + (static_cast<int64_t>(row) * HKV + kvh) * 64;
-#pragma unroll
-        for (int i = 0; i < 64; i += 8) store_bf16x8(pd + i, v + i);
-      }
-    }
+    QkvRow q;
+    load_qkv_row(ep, row, q);
+    qkv_head(ep, row, n_tile * (BN / 64) + ch, v, r, q);
   }
 }
 
@@ -847,20 +881,40 @@ __global__ void __launch_bounds__(kPThreads, 1)
       const int row = m0 + row_local;
       const bool row_ok = row < M;
       const float r = (row_ok && EPI != BIAS_ACT && EPI != ADD_RESID) ? row_rscale(ep, row) : 1.f;
+      // the epilogue's other global inputs do not depend on the accumulator: fetch them while the MMAs run
+      QkvRow qr;
+      uint4 xr[CPS][8];
+      if (EPI == QKV_ROPE && row_ok) load_qkv_row(ep, row, qr);
+      if (EPI == ADD_RESID && row_ok) {
+#pragma unroll
+        for (int cc = 0; cc < CPS; ++cc) {
+          const uint4* xp = reinterpret_cast<const uint4*>(ep.x + static_cast<int64_t>(row) * N + n_tile * BN +
+                                                           (set * CPS + cc) * 64);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) xr[cc][k] = xp[k];
+        }
+      }
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[ab], (i >> 1) & 1))) {
         if (lane == 0) raise_error(ERR_WAIT_ACCUM);
         break;
       }
       tc_fence_after();
       const uint32_t taddr = tmem_base + ab * BN + (static_cast<uint32_t>(quarter * 32) << 16);
-#pragma unroll 1
+#pragma unroll
       for (int cc = 0; cc < CPS; ++cc) {
         const int ch = set * CPS + cc;
         float v[64];
 #pragma unroll
         for (int q = 0; q < W; q += 16) tmem_ld16(taddr + chunk_col<BN, EPI>(ch, q), v + q);
         tmem_wait_ld();
-        if (row_ok) epi_chunk<BN, EPI>(ep, row, n_tile, ch, v, r, N);
+        if (row_ok) {
+          if (EPI == QKV_ROPE)
+            qkv_head(ep, row, n_tile * (BN / 64) + ch, v, r, qr);
+          else if (EPI == ADD_RESID)
+            add_resid_block(ep, row, n_tile * BN + ch * 64, v, xr[cc], N);
+          else
+            epi_chunk<BN, EPI>(ep, row, n_tile, ch, v, r, N);
+        }
       }
       tc_fence_before();
       __syncwarp();
