@@ -187,3 +187,26 @@ def test_config4_long_horizon_sampled_rows():
     ok, identical, stops = _compare(got[pick], ref, margin / 16.0)
     _report("config 4 (long horizon)", ok, identical, stops, steps)
     assert ok.all(), f"rows {np.array(pick)[~ok]} disagree before a low-margin step"
+
+
+def test_max_seq_len_prefix_and_decode():
+    """The decoder's whole position range: a 3000-frame prefix decoded for 1095 steps fills a cache of exactly
+    max_seq_len = 4096 positions (BOS at 3000, the last token at 4095: the last RoPE row and cache position),
+    beside a short chunk in the same batch.  Four long rows, so that some of them are compared up to the last
+    position (a row stops being compared at its first fp32 near-tie)."""
+    from viktor_b200 import DecodeEngine
+    steps, lens = 1095, [3000, 3000, 100, 3000, 3000]
+    model, port = _model(7, 1, seed=31)
+    frames = _frames(lens, seed=32)
+    eng = DecodeEngine(model, len(lens), steps, max(lens), max_homopolymer=None, device="cuda")
+    assert eng.cache.k.shape[2] == 4096
+    eng.bias[EOS] = float("-inf")
+    got = eng.generate(frames, lens, steps).cpu().numpy()
+    bias = np.zeros(7, np.float32)
+    bias[[0, 1, 2]] = -np.inf
+    ref, margin = port.generate(_rows(frames, lens, range(len(lens))), lens, steps, bias, None,
+                                return_margin=True)
+    ok, identical, stops = _compare(got, ref, margin)
+    _report("max_seq_len", ok, identical, stops, steps)
+    print("max_seq_len: steps compared per row", stops.tolist())
+    assert ok.all(), f"rows {np.arange(len(lens))[~ok]} disagree before a low-margin step"

@@ -240,7 +240,7 @@ def _sdpa_ref(q, k, v, lens, row0=0):
                                           attn_mask=mask)[:, :, 0]
 
 
-@pytest.mark.parametrize("S", [1300, 3200])
+@pytest.mark.parametrize("S", [1300, 3200, 4096])  # 4096: the decoder's max_seq_len
 def test_decode_attention(S):
     from viktor_b200.ops import decode_attention
     torch.manual_seed(S)
@@ -290,6 +290,28 @@ def test_prefill_attention():
         qb = q[t0:t0 + T].transpose(0, 1).float()[None]
         kb = kc[row0 + b, :T].transpose(0, 1).float().repeat_interleave(4, 0)[None]
         vb = vc[row0 + b, :T].transpose(0, 1).float().repeat_interleave(4, 0)[None]
+        ref = F.scaled_dot_product_attention(qb, kb, vb, is_causal=True)[0].transpose(0, 1)
+        err = (out[t0:t0 + T].float() - ref).abs().max()
+        assert err < 0.02, f"seq {b} (T={T}) err {err}"
+
+
+def test_prefill_attention_at_max_seq_len():
+    """A sequence of the decoder's maximum length (4096 positions: 32 query tiles, the diagonal tile full) next
+    to a single-token one, in a cache of exactly 4096 positions."""
+    from viktor_b200.ops import prefill_attention
+    torch.manual_seed(4)
+    lens = [4096, 1, 1500]
+    S, R = 4096, 3
+    n = sum(lens)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=DEV)
+    q = torch.randn(n, 8, 64, device=DEV, dtype=BF)
+    kc, vc = (torch.randn(R, S, 2, 64, device=DEV, dtype=BF) for _ in range(2))
+    out = prefill_attention(q, kc, vc, cu, max(lens))
+    for b, T in enumerate(lens):
+        t0 = int(cu[b])
+        qb = q[t0:t0 + T].transpose(0, 1).float()[None]
+        kb = kc[b, :T].transpose(0, 1).float().repeat_interleave(4, 0)[None]
+        vb = vc[b, :T].transpose(0, 1).float().repeat_interleave(4, 0)[None]
         ref = F.scaled_dot_product_attention(qb, kb, vb, is_causal=True)[0].transpose(0, 1)
         err = (out[t0:t0 + T].float() - ref).abs().max()
         assert err < 0.02, f"seq {b} (T={T}) err {err}"

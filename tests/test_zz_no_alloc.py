@@ -55,7 +55,8 @@ def _fp32_attention(q, k, v, lens):
 def test_noalloc_matches_workspace_entry_point_twice():
     from viktor_b200._lib import check_device_errors, load
     lib = load()
-    for seed, B, S in [(0, 256, 3200), (1, 48, 700)]:  # two calls in a row, different shapes
+    # calls in a row, different shapes; the last at the array's limit of 4096 positions
+    for seed, B, S in [(0, 256, 3200), (1, 48, 700), (3, 64, 4096)]:
         q, k, v, lens = _inputs(seed, B, S)
         ws = torch.zeros(lib.vk_decode_attention_workspace_bytes(B, S), dtype=torch.uint8, device="cuda")
         ref = _run("vk_decode_attention", q, k, v, lens, ws)
