@@ -210,3 +210,39 @@ def test_max_seq_len_prefix_and_decode():
     _report("max_seq_len", ok, identical, stops, steps)
     print("max_seq_len: steps compared per row", stops.tolist())
     assert ok.all(), f"rows {np.arange(len(lens))[~ok]} disagree before a low-margin step"
+
+
+def test_config6_2048_chunk_engine_batch():
+    """Configs 5 and 6 decode 2048 chunks in one engine batch: 16 prefill sub-batches of 128 and two decode
+    groups of 1024 rows.  Config-3 lengths and per-chunk decode lengths (round(128 x frames / 2048), then EOS);
+    sampled: the shortest and longest chunks, sub-batch boundaries and the rows either side of the group
+    boundary."""
+    from viktor_b200 import DecodeEngine
+    from viktor_b200.synthetic import varlen_prefix_lengths
+    B, steps = 2048, 128
+    model, port = _model(7, 1, seed=33)
+    lens = varlen_prefix_lengths(B, seed=34)
+    caps = [int(round(steps * n / 2048)) for n in lens]
+    frames = _frames(lens, seed=35)
+    eng = DecodeEngine(model, B, steps, 2048, prefill_batch=128, max_homopolymer=None, device="cuda")
+    eng.bias[EOS] = float("-inf")
+    eng.max_tokens.copy_(torch.tensor(caps))
+    got = eng.generate(frames, lens, None).cpu().numpy()
+    pick = sorted({int(np.argmin(lens)), int(np.argmax(lens)), 0, 127, 128, 895, 1023, 1024, 1025, 1920, B - 1})
+    bias = np.zeros(7, np.float32)
+    bias[[0, 1, 2]] = -np.inf
+    ref, margin = port.generate(_rows(frames, lens, pick), [lens[r] for r in pick], steps, bias, None,
+                                return_margin=True)
+    pc = [caps[r] for r in pick]
+    for i, c in enumerate(pc):  # the cap: EOS in column c, PAD after
+        if c < steps:
+            ref[i, c] = EOS
+            ref[i, c + 1:] = PAD
+    ok, identical, stops = _compare(got[pick], ref, margin, caps=pc)
+    _report("config 6 batch", ok, identical, stops, steps)
+    assert ok.all(), f"rows {np.array(pick)[~ok]} disagree before a low-margin step"
+    for b in range(B):  # every row: bases up to its cap, then EOS and PAD
+        c = caps[b]
+        assert (got[b, :min(c, steps)] >= 3).all()
+        if c < steps:
+            assert got[b, c] == EOS and (got[b, c + 1:] == PAD).all()
