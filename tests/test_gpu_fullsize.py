@@ -246,3 +246,29 @@ def test_config6_2048_chunk_engine_batch():
         assert (got[b, :min(c, steps)] >= 3).all()
         if c < steps:
             assert got[b, c] == EOS and (got[b, c + 1:] == PAD).all()
+
+
+def test_config2_full_size_int8_prefix():
+    """The opt-in int8 prefix mode at config 2 size (256 x 2048 frames, 256 steps, both decode groups): the
+    sampled rows agree with the fp32 port up to their first step whose top-2 margin is below 0.1, the mode's
+    own floor (twice the bf16 path's: the quantisation noise of the prefix)."""
+    from viktor_b200 import DecodeEngine
+    B, steps, floor = 256, 256, 0.1
+    model, port = _model(7, 1, seed=21)
+    lens = [2048] * B
+    frames = _frames(lens, seed=22)
+    eng = DecodeEngine(model, B, steps, 2048, max_homopolymer=None, device="cuda", kv_int8=True)
+    eng.bias[EOS] = float("-inf")
+    got = eng.generate(frames, lens, steps).cpu().numpy()
+    pick = list(range(3, B, 17))[:15]
+    bias = np.zeros(7, np.float32)
+    bias[[0, 1, 2]] = -np.inf
+    ref, margin = port.generate(_rows(frames, lens, pick), [2048] * len(pick), steps, bias, None, return_margin=True)
+    stops = []
+    for i in range(len(pick)):
+        low = np.where(np.nan_to_num(margin[i], nan=np.inf) < floor)[0]
+        stops.append(int(low[0]) if len(low) else steps)
+    ok = np.array([np.array_equal(got[r, :s], ref[i, :s]) for i, (r, s) in enumerate(zip(pick, stops))])
+    identical = (got[pick] == ref).all(1)
+    _report("config 2 int8 prefix", ok, identical, np.array(stops), steps)
+    assert ok.all(), f"rows {np.array(pick)[~ok]} disagree before a step of margin < {floor}"
